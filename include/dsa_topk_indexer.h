@@ -1,0 +1,106 @@
+/*
+ * C ABI of the B200 (sm_100a) DSA lightning-indexer top-K.
+ *
+ * All pointers are caller-owned, contiguous DEVICE buffers on the current
+ * CUDA device; every call is asynchronous on `stream` (a cudaStream_t, NULL
+ * for the legacy default stream). No entry point allocates device memory or
+ * synchronises the stream. Return value: DSA_OK or a DSA_ERR_* code.
+ *
+ * Layouts (the reference operator dsa_topk_indexer_fp8_h64_d128_topk2048_ps64):
+ *   q            [B, 64, 128]  FP8 e4m3 bytes
+ *   k_cache      [num_pages, 8448] bytes: per page 64 tokens x 128 e4m3
+ *                bytes (token-major), then 64 fp32 scales
+ *   weights      [B, 64]       fp32
+ *   seq_lens     [B]           int32
+ *   block_table  [B, max_pages] int32 physical page ids
+ *   topk_indices [B, 2048]     int32 physical slots page*64+offset, best
+ *                first (ties: smaller logical position first), -1 padded
+ */
+#ifndef DSA_TOPK_INDEXER_H
+#define DSA_TOPK_INDEXER_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSA_API __attribute__((visibility("default")))
+#else
+#define DSA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSA_OK 0
+#define DSA_ERR_INVALID_ARG 1 /* null pointer, negative size, bad stride  */
+#define DSA_ERR_MISALIGNED 2  /* q / k_cache not 16-byte aligned          */
+#define DSA_ERR_CUDA 3        /* a CUDA runtime/driver call failed        */
+#define DSA_ERR_NO_DEVICE 4   /* current device is not sm_100             */
+
+/* Bits of the per-device status word the kernels raise (sticky until read
+ * with clear != 0). */
+#define DSA_STATUS_WAIT_TIMEOUT 0x1u /* a pipeline wait gave up (kernel ended early) */
+#define DSA_STATUS_BAD_PAGE 0x2u     /* block_table held an id outside [0, num_pages) */
+#define DSA_STATUS_SEQ_CLAMPED 0x4u  /* seq_len > max_pages*64; clamped              */
+
+/*
+ * The indexer: scores every visible key of every request and writes the
+ * top-2048 physical slots. Replaces the reference host entry
+ * `launch_topk_c(q_index_fp8, k_index_cache_fp8, weights, seq_lens,
+ * block_table, topk_indices)` (solution/cuda/kernel.cu:818-887), without its
+ * N_max <= 8192 limit (kernel.cu:858-859).
+ */
+DSA_API int dsa_topk_indexer_launch(const void* q, const void* k_cache, const float* weights,
+                            const int32_t* seq_lens, const int32_t* block_table,
+                            int32_t* topk_indices, int64_t batch, int64_t max_pages,
+                            int64_t num_pages, void* stream);
+
+/*
+ * Scores only: scores[b, t] = sum_h w[b,h]*relu(scale[t]*q[b,h].k[t]) for
+ * t < seq_len[b], -inf for seq_len[b] <= t < score_stride. Same scoring path
+ * as the indexer; replaces the reference's fp32 `final_scores` intermediate
+ * written by fp8_mma_final_scores_kernel (solution/cuda/kernel.cu:209-452,
+ * buffer allocated at :847). Used for tolerance checks.
+ */
+DSA_API int dsa_topk_indexer_scores(const void* q, const void* k_cache, const float* weights,
+                            const int32_t* seq_lens, const int32_t* block_table, float* scores,
+                            int64_t score_stride, int64_t batch, int64_t max_pages,
+                            int64_t num_pages, void* stream);
+
+/*
+ * Key-range partial top-K for key-axis sharding of long sequences: request
+ * b only considers logical keys [key_begin, min(key_end, seq_len[b])).
+ * Writes its best 2048 candidates as (score, logical position) pairs,
+ * best first, padded with (-inf, -1). No counterpart in the reference (it has
+ * no multi-GPU path); it is the per-GPU half of the sharded indexer.
+ */
+DSA_API int dsa_topk_indexer_partial(const void* q, const void* k_cache, const float* weights,
+                             const int32_t* seq_lens, const int32_t* block_table,
+                             int64_t key_begin, int64_t key_end, float* cand_scores,
+                             int32_t* cand_pos, int64_t batch, int64_t max_pages,
+                             int64_t num_pages, void* stream);
+
+/*
+ * Merges `nparts` candidate lists per request ([nparts, B, 2048] each, as
+ * written by dsa_topk_indexer_partial) into the final top-2048 physical
+ * slots, with the indexer's order and padding rules. The second half of the
+ * sharded indexer; no counterpart in the reference.
+ */
+DSA_API int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* cand_pos, int64_t nparts,
+                           const int32_t* seq_lens, const int32_t* block_table,
+                           int32_t* topk_indices, int64_t batch, int64_t max_pages, void* stream);
+
+/* Reads (and optionally clears) the status word of device `device`.
+ * Synchronous with respect to the device. */
+DSA_API int dsa_topk_indexer_status(int device, uint32_t* status, int clear);
+
+/* Human-readable text for a DSA_* return code. */
+DSA_API const char* dsa_topk_indexer_error_string(int code);
+
+/* Number of kernel launches the last successful call on this host thread made. */
+DSA_API int dsa_topk_indexer_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSA_TOPK_INDEXER_H */

@@ -1,0 +1,161 @@
+"""B200 (sm_100a) DSA lightning-indexer top-K.
+
+Host-side mirror of the reference operator interface
+(`dsa_topk_indexer_fp8_h64_d128_topk2048_ps64`, entry point
+`kernel.cu::launch_topk_c`, destination-passing style; reference
+solution/cuda/kernel.cu:818-891). Every call goes through the C ABI of
+include/dsa_topk_indexer.h; there is no CPU fallback: if the CUDA library is
+missing, calls raise.
+
+The package directory name is not a Python identifier; import it with
+``importlib.import_module("karnbirkhera-mlsys2026-dsa_topk_indexer_b200")``.
+"""
+import ctypes
+
+from . import _lib
+from ._lib import (DSA_STATUS_BAD_PAGE, DSA_STATUS_SEQ_CLAMPED,  # noqa: F401
+                   DSA_STATUS_WAIT_TIMEOUT)
+
+HEADS = 64
+HEAD_DIM = 128
+PAGE_SIZE = 64
+PAGE_BYTES = 8448
+TOPK = 2048
+
+__all__ = ["launch_topk_c", "indexer_scores", "indexer_partial", "indexer_merge", "device_status",
+           "last_launch_count", "HEADS", "HEAD_DIM", "PAGE_SIZE", "PAGE_BYTES", "TOPK"]
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device):
+    return ctypes.c_void_p(_torch().cuda.current_stream(device).cuda_stream)
+
+
+def _require(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_inputs(q, kc, w, sl, bt):
+    torch = _torch()
+    dev = q.device
+    _require(dev.type == "cuda", "q_index_fp8 must be a CUDA tensor")
+    for name, t in (("k_index_cache_fp8", kc), ("weights", w), ("seq_lens", sl), ("block_table", bt)):
+        _require(t.device == dev, f"{name} must be on {dev}")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _require(q.is_contiguous(), "q_index_fp8 must be contiguous")
+    _require(q.element_size() == 1 and q.dim() == 3 and q.shape[1] == HEADS and q.shape[2] == HEAD_DIM,
+             "q_index_fp8 must be [B, 64, 128] fp8_e4m3 (or uint8)")
+    B = q.shape[0]
+    _require(kc.element_size() == 1 and kc.numel() % PAGE_BYTES == 0 and kc.numel() // PAGE_BYTES == kc.shape[0],
+             "k_index_cache_fp8 must be [num_pages, 64, 1, 132] (8448 bytes per page) of a 1-byte dtype")
+    _require(w.dtype == torch.float32 and tuple(w.shape) == (B, HEADS), "weights must be float32 [B, 64]")
+    _require(sl.dtype == torch.int32 and tuple(sl.shape) == (B,), "seq_lens must be int32 [B]")
+    _require(bt.dtype == torch.int32 and bt.dim() == 2 and bt.shape[0] == B and bt.shape[1] >= 1,
+             "block_table must be int32 [B, max_num_pages]")
+    return B, bt.shape[1], kc.shape[0]
+
+
+def launch_topk_c(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):
+    """Writes the top-2048 physical KV slots of every query into `topk_indices`.
+
+    Same tensor signature, argument meaning and destination-passing contract
+    as the reference entry point (solution/cuda/kernel.cu:818-824): rank
+    r < min(seq_len, 2048) holds block_table[b, pos // 64] * 64 + pos % 64 for
+    the r-th best logical position, the rest hold -1. Runs asynchronously on
+    the current CUDA stream. Raises RuntimeError on bad arguments (the
+    reference raises through TORCH_CHECK). Unlike the reference, there is no
+    max_num_pages * 64 <= 8192 limit.
+    """
+    torch = _torch()
+    B, max_pages, num_pages = _check_inputs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table)
+    _require(topk_indices.device == q_index_fp8.device and topk_indices.is_contiguous()
+             and topk_indices.dtype == torch.int32 and tuple(topk_indices.shape) == (B, TOPK),
+             "topk_indices must be a contiguous int32 [B, 2048] tensor on the same device")
+    lib = _lib.load()
+    with torch.cuda.device(q_index_fp8.device):
+        rc = lib.dsa_topk_indexer_launch(
+            _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
+            _ptr(topk_indices), B, max_pages, num_pages, _stream(q_index_fp8.device))
+    _lib.check(rc, "launch_topk_c")
+
+
+def indexer_scores(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, scores=None):
+    """fp32 scores [B, max_num_pages*64] of the same scoring path (-inf past seq_len)."""
+    torch = _torch()
+    B, max_pages, num_pages = _check_inputs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table)
+    if scores is None:
+        scores = torch.empty((B, max_pages * PAGE_SIZE), dtype=torch.float32, device=q_index_fp8.device)
+    _require(scores.dtype == torch.float32 and scores.is_contiguous() and scores.dim() == 2
+             and scores.shape[0] == B and scores.shape[1] >= max_pages * PAGE_SIZE,
+             "scores must be contiguous float32 [B, >= max_num_pages*64]")
+    lib = _lib.load()
+    with torch.cuda.device(q_index_fp8.device):
+        rc = lib.dsa_topk_indexer_scores(
+            _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
+            _ptr(scores), scores.shape[1], B, max_pages, num_pages, _stream(q_index_fp8.device))
+    _lib.check(rc, "indexer_scores")
+    return scores
+
+
+def indexer_partial(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, key_begin, key_end,
+                    cand_scores=None, cand_pos=None):
+    """Best 2048 (score, logical position) candidates among keys [key_begin, key_end)."""
+    torch = _torch()
+    B, max_pages, num_pages = _check_inputs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table)
+    dev = q_index_fp8.device
+    if cand_scores is None:
+        cand_scores = torch.empty((B, TOPK), dtype=torch.float32, device=dev)
+    if cand_pos is None:
+        cand_pos = torch.empty((B, TOPK), dtype=torch.int32, device=dev)
+    _require(cand_scores.is_contiguous() and cand_scores.dtype == torch.float32 and tuple(cand_scores.shape) == (B, TOPK)
+             and cand_pos.is_contiguous() and cand_pos.dtype == torch.int32 and tuple(cand_pos.shape) == (B, TOPK),
+             "cand_scores / cand_pos must be contiguous [B, 2048] float32 / int32")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.dsa_topk_indexer_partial(
+            _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
+            int(key_begin), int(key_end), _ptr(cand_scores), _ptr(cand_pos), B, max_pages, num_pages,
+            _stream(dev))
+    _lib.check(rc, "indexer_partial")
+    return cand_scores, cand_pos
+
+
+def indexer_merge(cand_scores, cand_pos, seq_lens, block_table, topk_indices=None):
+    """Merges [nparts, B, 2048] candidate lists into final top-2048 physical slots."""
+    torch = _torch()
+    _require(cand_scores.dim() == 3 and cand_scores.shape[2] == TOPK and cand_pos.shape == cand_scores.shape,
+             "candidates must be [nparts, B, 2048]")
+    nparts, B = cand_scores.shape[0], cand_scores.shape[1]
+    dev = cand_scores.device
+    if topk_indices is None:
+        topk_indices = torch.empty((B, TOPK), dtype=torch.int32, device=dev)
+    _require(block_table.dtype == torch.int32 and block_table.shape[0] == B and block_table.is_contiguous(),
+             "block_table must be contiguous int32 [B, max_num_pages]")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.dsa_topk_indexer_merge(_ptr(cand_scores.contiguous()), _ptr(cand_pos.contiguous()), nparts,
+                                        _ptr(seq_lens), _ptr(block_table), _ptr(topk_indices), B,
+                                        block_table.shape[1], _stream(dev))
+    _lib.check(rc, "indexer_merge")
+    return topk_indices
+
+
+def device_status(device=0, clear=True):
+    """Status bits the kernels raised on `device` since the last clear."""
+    v = ctypes.c_uint32(0)
+    _lib.check(_lib.load().dsa_topk_indexer_status(int(device), ctypes.byref(v), 1 if clear else 0),
+               "device_status")
+    return v.value
+
+
+def last_launch_count():
+    return _lib.load().dsa_topk_indexer_last_launch_count()

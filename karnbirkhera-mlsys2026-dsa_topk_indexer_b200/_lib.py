@@ -1,0 +1,56 @@
+"""ctypes binding of the C ABI declared in include/dsa_topk_indexer.h."""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdsa_topk_indexer.so")
+
+DSA_OK = 0
+DSA_ERR_INVALID_ARG = 1
+DSA_ERR_MISALIGNED = 2
+DSA_ERR_CUDA = 3
+DSA_ERR_NO_DEVICE = 4
+
+DSA_STATUS_WAIT_TIMEOUT = 0x1
+DSA_STATUS_BAD_PAGE = 0x2
+DSA_STATUS_SEQ_CLAMPED = 0x4
+
+# (name, restype, argtypes) for every function the header declares.
+_P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+SIGNATURES = [
+    ("dsa_topk_indexer_launch", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    ("dsa_topk_indexer_scores", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    ("dsa_topk_indexer_partial", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P]),
+    ("dsa_topk_indexer_merge", _I32, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _P]),
+    ("dsa_topk_indexer_status", _I32, [_I32, ctypes.POINTER(ctypes.c_uint32), _I32]),
+    ("dsa_topk_indexer_error_string", ctypes.c_char_p, [_I32]),
+    ("dsa_topk_indexer_last_launch_count", _I32, []),
+]
+
+_lib = None
+
+
+def load():
+    """Loads the CUDA library; raises if it has not been built (no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"DSA indexer CUDA library missing at {LIB_PATH}; build it with "
+                "__graft_entry__.build() (there is no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def error_string(code):
+    return load().dsa_topk_indexer_error_string(int(code)).decode()
+
+
+def check(code, what):
+    if code != DSA_OK:
+        raise RuntimeError(f"{what} failed: {error_string(code)} (code {code})")

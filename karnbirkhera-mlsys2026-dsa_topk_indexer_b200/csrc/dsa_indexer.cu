@@ -1,0 +1,367 @@
+// C-ABI implementation of the B200 DSA lightning-indexer top-K.
+// Kernels: indexer_kernel<mode> (indexer_kernel.cuh) and merge_kernel below.
+// Host responsibilities: argument checks, TMA tensor maps, cluster sizing,
+// launches. No device allocation, no stream synchronisation.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "dsa_topk_indexer.h"
+#include "indexer_kernel.cuh"
+
+namespace dsa {
+
+// --------------------------------------------------------------- merge kernel
+// Merges nparts best-first candidate lists (score, logical position) of one
+// request into its final top-2048 physical slots. One 256-thread CTA per
+// request; candidates stream through a 4096-key shared buffer that is
+// compacted to the exact best 2048 after every part.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeCap = 4096;
+constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 64;
+
+__global__ void __launch_bounds__(kMergeThreads, 1)
+    merge_kernel(const float* __restrict__ cand_scores, const int32_t* __restrict__ cand_pos, int nparts,
+                 const int32_t* __restrict__ block_table, int32_t* __restrict__ out, int batch, int max_pages) {
+  extern __shared__ __align__(16) uint8_t msmem[];
+  uint64_t* cand = reinterpret_cast<uint64_t*>(msmem);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(msmem + kMergeCap * 8);
+  uint32_t* misc = hist + 256;  // [0] count, [4..6] digit scan
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int b = blockIdx.x;
+  if (tid == 0) misc[0] = 0u;
+  __syncthreads();
+  uint64_t thr = 0;
+#pragma unroll 1
+  for (int j = 0; j < nparts; ++j) {
+    const int64_t row = (static_cast<int64_t>(j) * batch + b) * kTopK;
+#pragma unroll 1
+    for (int i0 = 0; i0 < kTopK; i0 += kMergeThreads) {
+      const int i = i0 + tid;
+      const int32_t pos = cand_pos[row + i];
+      const bool live = pos >= 0;
+      const uint64_t key = live ? pack_key(cand_scores[row + i], static_cast<uint32_t>(pos)) : 0ull;
+      const bool keep = live && key >= thr;
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        uint32_t base = 0;
+        if (lane == leader) base = atomicAdd(misc, static_cast<uint32_t>(__popc(m)));
+        base = __shfl_sync(0xFFFFFFFFu, base, leader);
+        if (keep) cand[base + __popc(m & lanemask_lt())] = key;
+      }
+      // Lists are best-first: once a whole chunk is rejected, so is the rest.
+      if (!__syncthreads_or(keep)) break;
+    }
+    __syncthreads();
+    const uint32_t n = misc[0];
+    __syncthreads();
+    if (n > static_cast<uint32_t>(kTopK)) {
+      thr = group_select<kMergeThreads, 0>(cand, n, kTopK, hist, misc + 4, tid);
+      group_compact<kMergeThreads, 0, kMergeCap / kMergeThreads>(cand, n, thr, misc, tid);
+    }
+  }
+  __syncthreads();
+  const uint32_t nsel = misc[0] < static_cast<uint32_t>(kTopK) ? misc[0] : static_cast<uint32_t>(kTopK);
+  for (uint32_t i = nsel + tid; i < static_cast<uint32_t>(kTopK); i += kMergeThreads) cand[i] = 0ull;
+  __syncthreads();
+  uint64_t v[8];
+  block_sort_desc_2048(cand, v);
+  const int32_t* bt_row = block_table + static_cast<int64_t>(b) * max_pages;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
+    const uint32_t pos = key_pos(v[r]);
+    out[static_cast<int64_t>(b) * kTopK + i] =
+        (i < nsel) ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
+  }
+}
+
+// Fills a float buffer (used for the -inf background of the score rows).
+__global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+thread_local int t_last_launches = 0;
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  bool ready = false;
+  int num_sms = 148;
+};
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_dev_mutex;
+
+// Per-device one-time set-up: architecture check and kernel attributes.
+int prepare_device(int* num_sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  DeviceInfo& d = g_devices[dev];
+  if (!d.ready) {
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return DSA_ERR_CUDA;
+    if (prop.major != 10 || prop.minor != 0) return DSA_ERR_NO_DEVICE;
+    d.num_sms = prop.multiProcessorCount;
+    const void* fns[3] = {reinterpret_cast<const void*>(&indexer_kernel<kModeTopK>),
+                          reinterpret_cast<const void*>(&indexer_kernel<kModeScores>),
+                          reinterpret_cast<const void*>(&indexer_kernel<kModePartial>)};
+    for (const void* f : fns) {
+      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+        return DSA_ERR_CUDA;
+    }
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&merge_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    d.ready = true;
+  }
+  *num_sms = d.num_sms;
+  return DSA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Tensor maps over the caller's buffers (encoded per call: they hold the
+// base address).
+int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_pages, CUtensorMap* tk,
+              CUtensorMap* ts, CUtensorMap* tq) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return DSA_ERR_CUDA;
+  std::memset(tk, 0, sizeof(*tk));
+  std::memset(ts, 0, sizeof(*ts));
+  std::memset(tq, 0, sizeof(*tq));
+  const cuuint32_t estr[3] = {1, 1, 1};
+  {  // page data: {128 bytes, 64 tokens, num_pages}, box = one page, 128-byte swizzle
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(kPage),
+                                static_cast<cuuint64_t>(num_pages)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(kPageBytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kDim), static_cast<cuuint32_t>(kPage), 1};
+    if (enc(tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(kcache), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return DSA_ERR_CUDA;
+  }
+  {  // page scales: {64 fp32, num_pages} starting at byte 8192 of page 0
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kPage), static_cast<cuuint64_t>(num_pages)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kPage), 1};
+    void* base = const_cast<uint8_t*>(static_cast<const uint8_t*>(kcache) + kPageData);
+    if (enc(ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return DSA_ERR_CUDA;
+  }
+  {  // q: {128 bytes, B*64 head rows}, box = one query (64 heads), 128-byte swizzle
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(batch * kHeads)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kDim)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kDim), static_cast<cuuint32_t>(kHeads)};
+    if (enc(tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return DSA_ERR_CUDA;
+  }
+  return DSA_OK;
+}
+
+// CTAs per request (the cluster size). The longest row gets about 32 tiles
+// (4096 keys) per CTA; small batches are spread wider so the grid covers the
+// GPU, but not below about 4 tiles per CTA.
+int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
+  const int64_t tiles = (span_pages + 1) / 2;
+  const int64_t g_len = (tiles + 31) / 32;
+  const int64_t g_fill = (2 * num_sms + batch - 1) / batch;
+  const int64_t g_floor = (tiles + 3) / 4;
+  int64_t g = g_fill < g_floor ? g_fill : g_floor;
+  if (g_len > g) g = g_len;
+  if (g < 1) g = 1;
+  if (g > 8) g = 8;
+  return static_cast<int>(g);
+}
+
+int check_common(const void* q, const void* kcache, const float* w, const int32_t* sl, const int32_t* bt,
+                 int64_t batch, int64_t max_pages, int64_t num_pages) {
+  if (batch < 0 || max_pages < 1 || num_pages < 1) return DSA_ERR_INVALID_ARG;
+  if (batch == 0) return DSA_OK;
+  if (!q || !kcache || !w || !sl || !bt) return DSA_ERR_INVALID_ARG;
+  if (num_pages > INT32_MAX || max_pages > INT32_MAX / kPage || batch > INT32_MAX / kHeads)
+    return DSA_ERR_INVALID_ARG;
+  if (!aligned16(q) || !aligned16(kcache)) return DSA_ERR_MISALIGNED;
+  return DSA_OK;
+}
+
+template <int kMode>
+int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, int64_t span_pages,
+                   cudaStream_t stream) {
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  CUtensorMap tk, ts, tq;
+  rc = make_maps(q, kcache, prm.batch, prm.num_pages, &tk, &ts, &tq);
+  if (rc != DSA_OK) return rc;
+  const int G = choose_cluster(prm.batch, span_pages, num_sms);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(G * static_cast<int64_t>(prm.batch)), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(G);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, prm) != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 1;
+  return DSA_OK;
+}
+
+IndexerParams base_params(const float* w, const int32_t* sl, const int32_t* bt, int64_t batch, int64_t max_pages,
+                          int64_t num_pages) {
+  IndexerParams p{};
+  p.seq_lens = sl;
+  p.block_table = bt;
+  p.weights = w;
+  p.num_pages = num_pages;
+  p.max_pages = static_cast<int32_t>(max_pages);
+  p.batch = static_cast<int32_t>(batch);
+  return p;
+}
+
+}  // namespace
+}  // namespace dsa
+
+using namespace dsa;
+
+extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const float* weights,
+                                       const int32_t* seq_lens, const int32_t* block_table, int32_t* topk_indices,
+                                       int64_t batch, int64_t max_pages, int64_t num_pages, void* stream) {
+  t_last_launches = 0;
+  int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
+  if (rc != DSA_OK || batch == 0) return rc;
+  if (!topk_indices) return DSA_ERR_INVALID_ARG;
+  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  p.out = topk_indices;
+  return launch_indexer<kModeTopK>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_topk_indexer_scores(const void* q, const void* k_cache, const float* weights,
+                                       const int32_t* seq_lens, const int32_t* block_table, float* scores,
+                                       int64_t score_stride, int64_t batch, int64_t max_pages, int64_t num_pages,
+                                       void* stream) {
+  t_last_launches = 0;
+  int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
+  if (rc != DSA_OK || batch == 0) return rc;
+  if (!scores || score_stride < max_pages * kPage) return DSA_ERR_INVALID_ARG;
+  // Columns past each row's length read -inf, as in the reference's
+  // final_scores (kernel.cu:433-434).
+  const int64_t n = score_stride * batch;
+  const int64_t blocks = (n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096;
+  fill_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      scores, n, -__builtin_huge_valf());
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  p.scores = scores;
+  p.score_stride = score_stride;
+  rc = launch_indexer<kModeScores>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
+  if (rc == DSA_OK) t_last_launches = 2;
+  return rc;
+}
+
+extern "C" int dsa_topk_indexer_partial(const void* q, const void* k_cache, const float* weights,
+                                        const int32_t* seq_lens, const int32_t* block_table, int64_t key_begin,
+                                        int64_t key_end, float* cand_scores, int32_t* cand_pos, int64_t batch,
+                                        int64_t max_pages, int64_t num_pages, void* stream) {
+  t_last_launches = 0;
+  int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
+  if (rc != DSA_OK || batch == 0) return rc;
+  if (!cand_scores || !cand_pos || key_begin < 0 || key_end < key_begin) return DSA_ERR_INVALID_ARG;
+  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  p.cand_scores = cand_scores;
+  p.cand_pos = cand_pos;
+  p.key_begin = key_begin;
+  p.key_end = key_end;
+  int64_t span = (key_end - key_begin + 2 * kPage - 1) / kPage;
+  if (span > max_pages) span = max_pages;
+  return launch_indexer<kModePartial>(q, k_cache, p, span, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* cand_pos, int64_t nparts,
+                                      const int32_t* seq_lens, const int32_t* block_table, int32_t* topk_indices,
+                                      int64_t batch, int64_t max_pages, void* stream) {
+  t_last_launches = 0;
+  if (batch < 0 || nparts < 1 || max_pages < 1 || max_pages > INT32_MAX / kPage || batch > INT32_MAX)
+    return DSA_ERR_INVALID_ARG;
+  if (batch == 0) return DSA_OK;
+  if (!cand_scores || !cand_pos || !seq_lens || !block_table || !topk_indices) return DSA_ERR_INVALID_ARG;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  merge_kernel<<<static_cast<unsigned>(batch), kMergeThreads, kMergeSmem, static_cast<cudaStream_t>(stream)>>>(
+      cand_scores, cand_pos, static_cast<int>(nparts), block_table, topk_indices, static_cast<int>(batch),
+      static_cast<int>(max_pages));
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 1;
+  return DSA_OK;
+}
+
+extern "C" int dsa_topk_indexer_status(int device, uint32_t* status, int clear) {
+  if (!status) return DSA_ERR_INVALID_ARG;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return DSA_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return DSA_ERR_CUDA;
+  unsigned int v = 0;
+  int rc = DSA_OK;
+  if (cudaMemcpyFromSymbol(&v, g_dsa_status, sizeof(v)) != cudaSuccess) rc = DSA_ERR_CUDA;
+  if (rc == DSA_OK && clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_dsa_status, &zero, sizeof(zero)) != cudaSuccess) rc = DSA_ERR_CUDA;
+  }
+  *status = v;
+  if (device != prev) cudaSetDevice(prev);
+  return rc;
+}
+
+extern "C" const char* dsa_topk_indexer_error_string(int code) {
+  switch (code) {
+    case DSA_OK:
+      return "ok";
+    case DSA_ERR_INVALID_ARG:
+      return "invalid argument (null pointer, negative or oversized dimension)";
+    case DSA_ERR_MISALIGNED:
+      return "q and k_cache must be 16-byte aligned";
+    case DSA_ERR_CUDA:
+      return "CUDA runtime or driver call failed";
+    case DSA_ERR_NO_DEVICE:
+      return "current device is not an sm_100 (B200) GPU";
+    default:
+      return "unknown error";
+  }
+}
+
+extern "C" int dsa_topk_indexer_last_launch_count(void) { return t_last_launches; }

@@ -1,0 +1,163 @@
+"""Seeded synthetic inputs with the shapes and value distributions of the five
+benchmark configurations, plus the paged index-K cache writer they use.
+
+The contest dataset (128 workloads) is not available here; these generators
+stand in for it. Cache format (reference methodology/framework/CLAUDE
+(16).md:493-537, solution/cuda/kernel.cu:22-25): a page is 8448 bytes,
+64 tokens x 128 e4m3 bytes, then 64 fp32 per-token scales.
+
+    q        N(0,1)*0.5, clipped to +-448, cast to e4m3
+    K        N(0,1), clipped, e4m3
+    scale    U[0.01, 0.1]   (config 4: log-uniform [1e-3, 1])
+    weights  U[0, 1] / 8
+"""
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+HEADS, DIM, PAGE, PAGE_BYTES, PAGE_DATA, TOPK = 64, 128, 64, 8448, 8192, 2048
+
+
+@dataclass
+class Workload:
+    name: str
+    q: torch.Tensor            # [B, 64, 128] float8_e4m3fn
+    k_cache: torch.Tensor      # [num_pages, 64, 1, 132] uint8
+    weights: torch.Tensor      # [B, 64] float32
+    seq_lens: torch.Tensor     # [B] int32
+    block_table: torch.Tensor  # [B, max_pages] int32
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def batch(self):
+        return self.q.shape[0]
+
+    @property
+    def max_pages(self):
+        return self.block_table.shape[1]
+
+    @property
+    def num_pages(self):
+        return self.k_cache.shape[0]
+
+    def kcache_bytes(self):
+        """Algorithmic K-cache bytes of one pass: sum(seq_len) * 132."""
+        sl = self.seq_lens.clamp(min=0, max=self.max_pages * PAGE).to(torch.int64)
+        return int(sl.sum()) * (DIM + 4)
+
+    def visible_keys(self):
+        sl = self.seq_lens.clamp(min=0, max=self.max_pages * PAGE).to(torch.int64)
+        return int(sl.sum())
+
+    def to(self, device):
+        return Workload(self.name, self.q.to(device), self.k_cache.to(device), self.weights.to(device),
+                        self.seq_lens.to(device), self.block_table.to(device), dict(self.meta))
+
+
+def e4m3(x):
+    return x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+
+def _gen(seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def write_pages(k_cache, pages, gen, scale_dist="uniform", chunk=32768):
+    """Fills the given physical pages with random e4m3 data and fp32 scales."""
+    flat = k_cache.view(k_cache.shape[0], PAGE_BYTES)
+    dev = k_cache.device
+    pages = pages.to(device=dev, dtype=torch.int64)
+    for s in range(0, pages.numel(), chunk):
+        idx = pages[s:s + chunk]
+        n = idx.numel()
+        data = e4m3(torch.randn((n, PAGE * DIM), generator=gen, device=dev)).view(torch.uint8)
+        u = torch.rand((n, PAGE), generator=gen, device=dev)
+        if scale_dist == "loguniform":
+            scale = torch.exp(math.log(1e-3) + u * (math.log(1.0) - math.log(1e-3)))
+        else:
+            scale = 0.01 + u * 0.09
+        flat[idx, :PAGE_DATA] = data
+        flat[idx, PAGE_DATA:] = scale.to(torch.float32).contiguous().view(torch.uint8).view(n, 256)
+
+
+def _queries(B, gen, device):
+    q = e4m3(torch.randn((B, HEADS, DIM), generator=gen, device=device) * 0.5)
+    w = torch.rand((B, HEADS), generator=gen, device=device) / 8.0
+    return q, w.to(torch.float32)
+
+
+def make_paged(name, seq_lens, pool_pages, seed, device="cpu", scale_dist="uniform", max_pages=None):
+    """Independent requests: request b owns a disjoint run of pages taken in
+    order from a shuffled pool. Unused block-table entries hold page 0 (a valid
+    id, so readers that touch them stay in bounds)."""
+    gen = _gen(seed, device)
+    seq_lens = torch.as_tensor(seq_lens, dtype=torch.int32)
+    B = seq_lens.numel()
+    npages = [(int(s) + PAGE - 1) // PAGE for s in seq_lens.tolist()]
+    if max_pages is None:
+        max_pages = max(1, max(npages) if npages else 1)
+    need = sum(npages)
+    if need > pool_pages:
+        raise ValueError(f"{name}: needs {need} pages, pool has {pool_pages}")
+    perm = torch.randperm(pool_pages, generator=_gen(seed + 1, "cpu"))
+    bt = torch.zeros((B, max_pages), dtype=torch.int32)
+    off = 0
+    for b, n in enumerate(npages):
+        bt[b, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    k_cache = torch.zeros((pool_pages, PAGE, 1, DIM + 4), dtype=torch.uint8, device=device)
+    write_pages(k_cache, perm[:need], gen, scale_dist)
+    q, w = _queries(B, gen, device)
+    return Workload(name, q, k_cache, w, seq_lens.to(device), bt.to(device), {"pool_pages": pool_pages})
+
+
+def make_shared(name, n_queries, total_keys, pool_pages, seed, device="cpu", scale_dist="uniform"):
+    """One sequence: query i is the (total_keys - n_queries + i)-th token and
+    sees keys 0..that position (causal); every row shares one block-table row
+    over `pool_pages` shuffled pages."""
+    gen = _gen(seed, device)
+    n_pages = (total_keys + PAGE - 1) // PAGE
+    perm = torch.randperm(pool_pages, generator=_gen(seed + 1, "cpu"))[:n_pages].to(torch.int32)
+    bt = perm.view(1, -1).expand(n_queries, -1).contiguous()
+    first = total_keys - n_queries
+    seq_lens = torch.arange(first + 1, total_keys + 1, dtype=torch.int32)
+    k_cache = torch.zeros((pool_pages, PAGE, 1, DIM + 4), dtype=torch.uint8, device=device)
+    write_pages(k_cache, perm.to(torch.int64), gen, scale_dist)
+    q, w = _queries(n_queries, gen, device)
+    return Workload(name, q, k_cache, w, seq_lens.to(device), bt.to(device), {"pool_pages": pool_pages})
+
+
+def config(idx, device="cpu", seed=None, scale_batch=1.0):
+    """BASELINE.json configs[idx]. Seeds default to idx. `scale_batch` < 1
+    shrinks the batch (parity tests at reduced size; never used for bench)."""
+    seed = idx if seed is None else seed
+    if idx == 0:
+        w = make_paged("cfg0_decode_b1", [4096], 64, seed, device)
+        return w
+    if idx == 1:
+        g = _gen(seed + 100, "cpu")
+        B = max(1, int(round(64 * scale_batch)))
+        u = torch.rand(B, generator=g, dtype=torch.float64)
+        sl = torch.exp(math.log(512) + u * (math.log(32768) - math.log(512))).floor().to(torch.int32)
+        return make_paged("cfg1_decode_b64", sl, 40000, seed, device)
+    if idx == 2:
+        g = _gen(seed + 100, "cpu")
+        B = max(1, int(round(512 * scale_batch)))
+        sl = torch.randint(16384, 131072 + 1, (B,), generator=g, dtype=torch.int64).to(torch.int32)
+        pool = 1200000 if B == 512 else max(2048 * B, int(1200000 * B / 512))
+        return make_paged("cfg2_decode_b512", sl, pool, seed, device, max_pages=2048)
+    if idx == 3:
+        return make_shared("cfg3_prefill_8k", 8192, 8192, 128, seed, device)
+    if idx == 4:
+        return make_shared("cfg4_longctx_128k", 2048, 131072, 2048, seed, device, scale_dist="loguniform")
+    raise ValueError(idx)
+
+
+def custom(seq_lens, pool_pages=None, seed=0, device="cpu", max_pages=None, scale_dist="uniform"):
+    """Small ad-hoc workload for tests."""
+    need = sum((int(s) + PAGE - 1) // PAGE for s in seq_lens)
+    pool = pool_pages if pool_pages is not None else max(1, need + 3)
+    return make_paged("custom", seq_lens, pool, seed, device, scale_dist, max_pages=max_pages)

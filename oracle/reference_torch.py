@@ -1,0 +1,89 @@
+"""PyTorch CPU restatement of the reference operator's definition.
+
+TEST INFRASTRUCTURE ONLY (checker, golden-vector generator and the timed
+CPU baseline of bench.py). It follows, step by step:
+  - the grader's dequantisation quoted in the reference at
+    methodology/framework/CLAUDE (16).md:505-517 (blocked page: 8192 data
+    bytes viewed as e4m3 [64,128], 256 scale bytes viewed as fp32 [64,1];
+    K_deq = data.to(f32) * scale);
+  - the per-request math of methodology/checkpoints/kernel_naive.cu:92-113
+    (scores = q_b @ K.T in fp32, relu(scores) * w[:, None], sum over heads,
+    top min(2048, seq_len), translate to block_table[b, pos>>6]*64 + (pos&63),
+    -1 elsewhere);
+  - the stable descending order of solution/cuda/kernel.cu:511 for ties
+    (torch.sort(..., stable=True)).
+Sequences are processed one at a time, or in query chunks sharing one block
+table row (causal prefill), so large configs fit in host memory.
+"""
+import torch
+
+PAGE, PAGE_BYTES, TOPK = 64, 8448, 2048
+
+
+def dequant_pages(k_cache_u8, pages):
+    """K_deq [len(pages)*64, 128] fp32 for the given physical pages."""
+    kv = k_cache_u8.view(torch.uint8).reshape(k_cache_u8.shape[0], PAGE_BYTES)[pages.long()]
+    n = kv.shape[0]
+    data = kv[:, :PAGE * 128].contiguous().view(torch.float8_e4m3fn).view(n, PAGE, 128)
+    scale = kv[:, PAGE * 128:].contiguous().view(torch.float32).view(n, PAGE, 1)
+    return (data.to(torch.float32) * scale).reshape(n * PAGE, 128)
+
+
+def request_scores(q_b, k_deq, w_b):
+    """fp32 final scores [len] of one query over dequantised keys."""
+    s = q_b.to(torch.float32) @ k_deq.T           # [64, len]
+    return (torch.relu(s) * w_b[:, None]).sum(0)  # [len]
+
+
+def topk_translate(final, bt_row):
+    n = final.shape[0]
+    k = min(TOPK, n)
+    out = torch.full((TOPK,), -1, dtype=torch.int32)
+    if k > 0:
+        _, idx = torch.sort(final, descending=True, stable=True)
+        idx = idx[:k]
+        out[:k] = (bt_row[(idx // PAGE)] * PAGE + (idx % PAGE)).to(torch.int32)
+    return out
+
+
+@torch.no_grad()
+def indexer(q, k_cache, weights, seq_lens, block_table, return_scores=False):
+    q, k_cache, weights = q.cpu(), k_cache.cpu(), weights.cpu()
+    seq_lens, block_table = seq_lens.cpu(), block_table.cpu()
+    B, max_pages = block_table.shape
+    out = torch.full((B, TOPK), -1, dtype=torch.int32)
+    rows = []
+    for b in range(B):
+        sl = max(0, min(int(seq_lens[b]), max_pages * PAGE))
+        if sl == 0:
+            rows.append(torch.empty(0))
+            continue
+        npg = (sl + PAGE - 1) // PAGE
+        kd = dequant_pages(k_cache, block_table[b, :npg])[:sl]
+        final = request_scores(q[b], kd, weights[b])
+        out[b] = topk_translate(final, block_table[b])
+        if return_scores:
+            rows.append(final)
+    return (out, rows) if return_scores else out
+
+
+@torch.no_grad()
+def indexer_shared_causal(q, k_cache, weights, seq_lens, block_table, chunk=256):
+    """Same results as indexer() when every row shares block_table[0] (the
+    prefill configs), computed in query chunks with one dequantisation."""
+    q, k_cache, weights = q.cpu(), k_cache.cpu(), weights.cpu()
+    seq_lens, block_table = seq_lens.cpu(), block_table.cpu()
+    B, max_pages = block_table.shape
+    sl_all = seq_lens.clamp(0, max_pages * PAGE)
+    L = int(sl_all.max()) if B else 0
+    npg = (L + PAGE - 1) // PAGE
+    kd = dequant_pages(k_cache, block_table[0, :npg])[:L]
+    out = torch.full((B, TOPK), -1, dtype=torch.int32)
+    for s in range(0, B, chunk):
+        e = min(B, s + chunk)
+        lmax = int(sl_all[s:e].max())
+        sc = torch.einsum("bhd,td->bht", q[s:e].to(torch.float32), kd[:lmax])
+        final = (torch.relu(sc) * weights[s:e, :, None]).sum(1)  # [n, lmax]
+        for i in range(e - s):
+            out[s + i] = topk_translate(final[i, :int(sl_all[s + i])], block_table[s + i])
+    return out

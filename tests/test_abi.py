@@ -1,0 +1,71 @@
+"""CPU: the C-ABI library loads, exports every symbol include/*.h declares,
+and rejects bad arguments before touching the GPU."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from conftest import ROOT, package
+
+
+def _declared():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        names += re.findall(r"DSA_API\s+[\w\s\*]+?\b(dsa_\w+)\s*\(", open(h).read())
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    pkg = package()
+    if not os.path.exists(pkg._lib.LIB_PATH):
+        from importlib import import_module
+        import_module(pkg.__name__ + ".build").build_cuda()
+    return pkg._lib.load()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("dsa_topk_indexer_launch", "dsa_topk_indexer_scores", "dsa_topk_indexer_partial",
+              "dsa_topk_indexer_merge", "dsa_topk_indexer_status", "dsa_topk_indexer_error_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(package()._lib.LIB_PATH)
+    for n in _declared():
+        assert hasattr(raw, n), f"{n} declared in include/ but not exported"
+
+
+def test_ctypes_signatures_cover_header(lib):
+    assert {s[0] for s in package()._lib.SIGNATURES} == set(_declared())
+
+
+def test_argument_errors_without_gpu(lib):
+    P = ctypes.c_void_p
+    ok = P(16)
+    # null pointers / bad sizes are rejected before any CUDA call
+    assert lib.dsa_topk_indexer_launch(None, ok, ok, ok, ok, ok, 4, 8, 16, None) == 1
+    assert lib.dsa_topk_indexer_launch(ok, ok, ok, ok, ok, ok, -1, 8, 16, None) == 1
+    assert lib.dsa_topk_indexer_launch(ok, ok, ok, ok, ok, ok, 4, 0, 16, None) == 1
+    assert lib.dsa_topk_indexer_launch(P(17), ok, ok, ok, ok, ok, 4, 8, 16, None) == 2
+    assert lib.dsa_topk_indexer_scores(ok, ok, ok, ok, ok, ok, 10, 4, 8, 16, None) == 1  # stride < 8*64
+    assert lib.dsa_topk_indexer_partial(ok, ok, ok, ok, ok, 10, 5, ok, ok, 4, 8, 16, None) == 1
+    assert lib.dsa_topk_indexer_merge(ok, ok, 0, ok, ok, ok, 4, 8, None) == 1
+    # empty batch is a no-op
+    assert lib.dsa_topk_indexer_launch(None, None, None, None, None, None, 0, 8, 16, None) == 0
+    assert b"aligned" in lib.dsa_topk_indexer_error_string(2)
+
+
+def test_torch_wrapper_validates_before_launch(pkg):
+    import torch
+    q = torch.zeros((2, 64, 128), dtype=torch.uint8)
+    kc = torch.zeros((4, 64, 1, 132), dtype=torch.uint8)
+    w = torch.zeros((2, 64))
+    sl = torch.zeros(2, dtype=torch.int32)
+    bt = torch.zeros((2, 2), dtype=torch.int32)
+    out = torch.zeros((2, 2048), dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        pkg.launch_topk_c(q, kc, w, sl, bt, out)

@@ -1,0 +1,236 @@
+"""GPU parity: the CUDA path through the C ABI against the oracle.
+
+Bar: scores within rtol 1e-2 / atol 1e-3 (tests/parity.py), index sets equal
+except at near-ties of the k-th score, -1 padding bit-exact; known-answer
+cases bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_names, load_golden, workloads
+from parity import check_all
+
+pytestmark = pytest.mark.gpu
+RTOL, ATOL = 1e-2, 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda(pkg):
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    pkg.device_status(0, clear=True)
+    yield
+    torch.cuda.synchronize()
+
+
+def run(pkg, w, stream=None):
+    d = w.to("cuda")
+    out = torch.full((w.batch, 2048), -7, dtype=torch.int32, device="cuda")
+    if stream is None:
+        pkg.launch_topk_c(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, out)
+    else:
+        with torch.cuda.stream(stream):
+            pkg.launch_topk_c(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, out)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def oracle_rows(w):
+    sc = oracle.scores(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
+    sl = np.clip(w.seq_lens.numpy(), 0, w.max_pages * 64)
+    return [sc[b, :sl[b]] for b in range(w.batch)], sc
+
+
+def assert_parity(pkg, w, out=None):
+    out = run(pkg, w) if out is None else out
+    ref = oracle.indexer(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
+    rows, _ = oracle_rows(w)
+    fails = check_all(out, ref, rows, w.seq_lens.numpy(), w.block_table.numpy(), w.num_pages)
+    assert not fails, fails[:5]
+    assert pkg.device_status(0) == 0
+    return out, ref
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden(pkg, name):
+    w, expected, rows = load_golden(name)
+    out = run(pkg, w)
+    fails = check_all(out, expected, rows, w.seq_lens.numpy(), w.block_table.numpy(), w.num_pages)
+    assert not fails, fails[:5]
+    assert pkg.device_status(0) == 0
+
+
+def test_kat_bit_exact(pkg):
+    """Diagonal tiles (the reference's tcgen05 probe pattern): exact scores,
+    exact ties broken by the smaller position."""
+    w, expected, _ = load_golden("kat_diag")
+    out = run(pkg, w)
+    assert np.array_equal(out, expected)
+
+
+def test_kat_scores_exact(pkg):
+    w, _, rows = load_golden("kat_diag")
+    d = w.to("cuda")
+    sc = pkg.indexer_scores(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table).cpu().numpy()
+    assert np.array_equal(sc[0, :128], rows[0])
+
+
+@pytest.mark.parametrize("sls", [[4096], [1, 63, 64, 65, 127, 128, 129], [2047, 2048, 2049, 0, 300],
+                                 [40000, 7, 130000]])
+def test_scores_within_tolerance(pkg, sls):
+    W = workloads()
+    w = W.custom(sls, seed=len(sls))
+    d = w.to("cuda")
+    got = pkg.indexer_scores(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table).cpu().numpy()
+    _, ref = oracle_rows(w)
+    fin = np.isfinite(ref)
+    np.testing.assert_allclose(got[fin], ref[fin], rtol=RTOL, atol=ATOL)
+    assert np.array_equal(np.isneginf(got), ~fin)
+
+
+@pytest.mark.parametrize("sls", [[0], [1], [5, 0, 77], [64 * 3 + 1] * 5, [2047, 2048, 2049],
+                                 [8191, 8192, 8193], [33000], [131072]])
+def test_edge_lengths(pkg, sls):
+    W = workloads()
+    assert_parity(pkg, W.custom(sls, seed=7))
+
+
+def test_unused_block_table_tail(pkg):
+    """max_num_pages far above the longest row; tail entries are never read."""
+    W = workloads()
+    w = W.custom([100, 3000], seed=8, max_pages=400)
+    w.block_table[:, 100:] = -12345  # invalid ids past every row's pages
+    assert_parity(pkg, w)
+
+
+def test_config0(pkg):
+    assert_parity(pkg, workloads().config(0))
+
+
+def test_config1(pkg):
+    assert_parity(pkg, workloads().config(1))
+
+
+def test_config2_subset(pkg):
+    """Config 2 rows (16k..131k keys) at reduced batch; full size is covered
+    by the property test below."""
+    assert_parity(pkg, workloads().config(2, scale_batch=8 / 512))
+
+
+def _rows(w, idx):
+    idx = torch.as_tensor(idx)
+    return type(w)(w.name, w.q[idx].contiguous(), w.k_cache, w.weights[idx].contiguous(),
+                   w.seq_lens[idx].contiguous(), w.block_table[idx].contiguous())
+
+
+def test_config3_full(pkg):
+    assert_parity(pkg, workloads().config(3))
+
+
+def test_config4_rows(pkg):
+    w = workloads().config(4)
+    assert_parity(pkg, _rows(w, list(range(0, 2048, 128)) + [2047]))
+
+
+def test_config4_full_properties_and_sample(pkg):
+    w = workloads().config(4)
+    out = run(pkg, w)
+    assert (out >= 0).all()  # every row has >= 2048 visible keys
+    slots = np.sort(out, axis=1)
+    assert (np.diff(slots, axis=1) > 0).all()  # unique per row
+    sample = [0, 1, 777, 2046, 2047]
+    sw = _rows(w, sample)
+    assert_parity(pkg, sw, out=out[sample])
+
+
+def test_config2_full_properties(pkg):
+    """Full config 2 (512 rows, ~4.98 GB of K) on the GPU: structural
+    properties on every row, oracle parity on a sample of rows."""
+    w = workloads().config(2, device="cuda")
+    out = torch.empty((w.batch, 2048), dtype=torch.int32, device="cuda")
+    pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, out)
+    torch.cuda.synchronize()
+    assert pkg.device_status(0) == 0
+    o = out.cpu().numpy()
+    bt = w.block_table.cpu().numpy()
+    assert (o >= 0).all()
+    assert (np.diff(np.sort(o, axis=1), axis=1) > 0).all()
+    sl = w.seq_lens.cpu().numpy()
+    for b in range(w.batch):  # every slot belongs to the row's own pages
+        assert np.isin(o[b] // 64, bt[b, :(sl[b] + 63) // 64]).all()
+    sample = [0, 255, 511]
+    # Oracle on a compacted copy (only the sampled rows' pages, renumbered),
+    # mapped back to the original physical slots.
+    used = np.unique(np.concatenate([bt[b, :(sl[b] + 63) // 64] for b in sample]))
+    remap = {int(p): j for j, p in enumerate(used)}
+    kc = w.k_cache[torch.from_numpy(used).long().cuda()].cpu()
+    bt_c = np.zeros((len(sample), bt.shape[1]), dtype=np.int32)
+    for i, b in enumerate(sample):
+        n = (sl[b] + 63) // 64
+        bt_c[i, :n] = [remap[int(p)] for p in bt[b, :n]]
+    sw = type(w)("cfg2_sample", w.q[sample].cpu(), kc, w.weights[sample].cpu(), w.seq_lens[sample].cpu(),
+                 torch.from_numpy(bt_c))
+    ref_c = oracle.indexer(sw.q, sw.k_cache, sw.weights, sw.seq_lens, sw.block_table)
+    ref = np.where(ref_c >= 0, used[np.maximum(ref_c, 0) // 64] * 64 + ref_c % 64, -1)
+    rows, _ = oracle_rows(sw)
+    fails = check_all(o[sample], ref, rows, sl[sample], bt[sample], w.num_pages)
+    assert not fails, fails[:5]
+    del w
+    torch.cuda.empty_cache()
+
+
+def test_partial_merge_equals_direct(pkg):
+    """Key-axis sharding: per-range partial top-K + merge is bit-identical to
+    the one-shot indexer (same scores, same exact selection)."""
+    w = workloads().custom([50000, 131072, 3000, 0], seed=9)
+    d = w.to("cuda")
+    direct = run(pkg, w)
+    L = 131072
+    parts = 4
+    bounds = [(L * i // parts, L * (i + 1) // parts) for i in range(parts)]
+    cs = torch.empty((parts, w.batch, 2048), dtype=torch.float32, device="cuda")
+    cp = torch.empty((parts, w.batch, 2048), dtype=torch.int32, device="cuda")
+    for i, (lo, hi) in enumerate(bounds):
+        pkg.indexer_partial(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, lo, hi, cs[i], cp[i])
+    merged = pkg.indexer_merge(cs, cp, d.seq_lens, d.block_table)
+    torch.cuda.synchronize()
+    assert np.array_equal(merged.cpu().numpy(), direct)
+
+
+def test_partial_unaligned_ranges(pkg):
+    w = workloads().custom([9000, 5000], seed=10)
+    d = w.to("cuda")
+    direct = run(pkg, w)
+    bounds = [(0, 1000), (1000, 4097), (4097, 9000)]
+    cs = torch.empty((3, 2, 2048), dtype=torch.float32, device="cuda")
+    cp = torch.empty((3, 2, 2048), dtype=torch.int32, device="cuda")
+    for i, (lo, hi) in enumerate(bounds):
+        pkg.indexer_partial(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, lo, hi, cs[i], cp[i])
+    merged = pkg.indexer_merge(cs, cp, d.seq_lens, d.block_table)
+    torch.cuda.synchronize()
+    assert np.array_equal(merged.cpu().numpy(), direct)
+
+
+def test_deterministic_and_side_stream(pkg):
+    w = workloads().config(1, scale_batch=0.25)
+    a = run(pkg, w)
+    b = run(pkg, w, stream=torch.cuda.Stream())
+    assert np.array_equal(a, b)
+
+
+def test_bad_page_id_flags_status(pkg):
+    """An out-of-range page id is zero-filled by the TMA bounds check and
+    reported in the status word; the kernel does not fault."""
+    w = workloads().custom([3000], seed=12)
+    w.block_table[0, 5] = w.num_pages + 1000
+    run(pkg, w)
+    assert pkg.device_status(0) & pkg.DSA_STATUS_BAD_PAGE
+
+
+def test_seq_len_clamped_flags_status(pkg):
+    w = workloads().custom([1000], seed=13)
+    w.seq_lens[0] = 5000  # longer than max_pages * 64 = 1024
+    out = run(pkg, w)
+    assert pkg.device_status(0) & pkg.DSA_STATUS_SEQ_CLAMPED
+    assert (out[0, :1024] >= 0).all() and (out[0, 1024:] == -1).all()
