@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -192,6 +193,11 @@ int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_page
 // (4096 keys) per CTA; small batches are spread wider so the grid covers the
 // GPU, but not below about 4 tiles per CTA.
 int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
+  // DSA_TOPK_CLUSTER=<1..8> overrides the choice (tuning and tests).
+  if (const char* env = std::getenv("DSA_TOPK_CLUSTER")) {
+    const int g = std::atoi(env);
+    if (g >= 1 && g <= 8) return g;
+  }
   const int64_t tiles = (span_pages + 1) / 2;
   const int64_t g_len = (tiles + 31) / 32;
   const int64_t g_fill = (2 * num_sms + batch - 1) / batch;

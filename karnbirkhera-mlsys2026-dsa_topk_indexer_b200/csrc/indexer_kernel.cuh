@@ -94,7 +94,7 @@ __device__ unsigned int g_dsa_status;
 // score = sum_h w_h * relu(scale * acc_h), evaluated as
 // |scale| * sum_h w_h * relu(sign(scale) * acc_h): the scale is applied once
 // per key instead of once per head (exact up to fp32 rounding, any sign).
-__device__ __forceinline__ float head_reduce(const uint32_t (&a)[32], const uint32_t (&c)[32], const float* s_w,
+__device__ __forceinline__ float head_reduce(const uint32_t (&acc)[64], const float* s_w,
                                              float scale) {
   const float4* w4 = reinterpret_cast<const float4*>(s_w);
   float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
@@ -102,36 +102,36 @@ __device__ __forceinline__ float head_reduce(const uint32_t (&a)[32], const uint
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 w = w4[j];
-      s0 = fmaf(w.x, fmaxf(__uint_as_float(a[4 * j + 0]), 0.f), s0);
-      s1 = fmaf(w.y, fmaxf(__uint_as_float(a[4 * j + 1]), 0.f), s1);
-      s2 = fmaf(w.z, fmaxf(__uint_as_float(a[4 * j + 2]), 0.f), s2);
-      s3 = fmaf(w.w, fmaxf(__uint_as_float(a[4 * j + 3]), 0.f), s3);
+      s0 = fmaf(w.x, fmaxf(__uint_as_float(acc[4 * j + 0]), 0.f), s0);
+      s1 = fmaf(w.y, fmaxf(__uint_as_float(acc[4 * j + 1]), 0.f), s1);
+      s2 = fmaf(w.z, fmaxf(__uint_as_float(acc[4 * j + 2]), 0.f), s2);
+      s3 = fmaf(w.w, fmaxf(__uint_as_float(acc[4 * j + 3]), 0.f), s3);
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float4 w = w4[8 + j];
-      s0 = fmaf(w.x, fmaxf(__uint_as_float(c[4 * j + 0]), 0.f), s0);
-      s1 = fmaf(w.y, fmaxf(__uint_as_float(c[4 * j + 1]), 0.f), s1);
-      s2 = fmaf(w.z, fmaxf(__uint_as_float(c[4 * j + 2]), 0.f), s2);
-      s3 = fmaf(w.w, fmaxf(__uint_as_float(c[4 * j + 3]), 0.f), s3);
+      s0 = fmaf(w.x, fmaxf(__uint_as_float(acc[32 + 4 * j + 0]), 0.f), s0);
+      s1 = fmaf(w.y, fmaxf(__uint_as_float(acc[32 + 4 * j + 1]), 0.f), s1);
+      s2 = fmaf(w.z, fmaxf(__uint_as_float(acc[32 + 4 * j + 2]), 0.f), s2);
+      s3 = fmaf(w.w, fmaxf(__uint_as_float(acc[32 + 4 * j + 3]), 0.f), s3);
     }
     return ((s0 + s1) + (s2 + s3)) * scale;
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 w = w4[j];
-    s0 = fmaf(w.x, fmaxf(-__uint_as_float(a[4 * j + 0]), 0.f), s0);
-    s1 = fmaf(w.y, fmaxf(-__uint_as_float(a[4 * j + 1]), 0.f), s1);
-    s2 = fmaf(w.z, fmaxf(-__uint_as_float(a[4 * j + 2]), 0.f), s2);
-    s3 = fmaf(w.w, fmaxf(-__uint_as_float(a[4 * j + 3]), 0.f), s3);
+    s0 = fmaf(w.x, fmaxf(-__uint_as_float(acc[4 * j + 0]), 0.f), s0);
+    s1 = fmaf(w.y, fmaxf(-__uint_as_float(acc[4 * j + 1]), 0.f), s1);
+    s2 = fmaf(w.z, fmaxf(-__uint_as_float(acc[4 * j + 2]), 0.f), s2);
+    s3 = fmaf(w.w, fmaxf(-__uint_as_float(acc[4 * j + 3]), 0.f), s3);
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 w = w4[8 + j];
-    s0 = fmaf(w.x, fmaxf(-__uint_as_float(c[4 * j + 0]), 0.f), s0);
-    s1 = fmaf(w.y, fmaxf(-__uint_as_float(c[4 * j + 1]), 0.f), s1);
-    s2 = fmaf(w.z, fmaxf(-__uint_as_float(c[4 * j + 2]), 0.f), s2);
-    s3 = fmaf(w.w, fmaxf(-__uint_as_float(c[4 * j + 3]), 0.f), s3);
+    s0 = fmaf(w.x, fmaxf(-__uint_as_float(acc[32 + 4 * j + 0]), 0.f), s0);
+    s1 = fmaf(w.y, fmaxf(-__uint_as_float(acc[32 + 4 * j + 1]), 0.f), s1);
+    s2 = fmaf(w.z, fmaxf(-__uint_as_float(acc[32 + 4 * j + 2]), 0.f), s2);
+    s3 = fmaf(w.w, fmaxf(-__uint_as_float(acc[32 + 4 * j + 3]), 0.f), s3);
   }
   return ((s0 + s1) + (s2 + s3)) * (-scale);
 }
@@ -149,7 +149,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kOffHist);
   uint32_t* tot = reinterpret_cast<uint32_t*>(smem + kOffTot);
   float* s_w = reinterpret_cast<float*>(smem + kOffW);
-  const float* s_scale = reinterpret_cast<const float*>(smem + kOffScale);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc);
   uint32_t* misc_nv = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = misc + kMiscAbort;
@@ -286,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         aborted = true;
         break;
       }
+      __syncwarp();
       ptx::tc_fence_after();
       if (lane == 0) {
         const uint64_t adesc = ptx::sw128_kmajor_desc(base_addr + kOffK + s * 16384);
@@ -317,7 +317,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         aborted = true;
         break;
       }
-      const float scale = s_scale[s * kTileKeys + row];
+      // The scale is read with a generic-proxy load, and the producer's next
+      // TMA into this stage writes through the async proxy as soon as the MMA
+      // commit and all four epilogue warps have arrived. Without the proxy
+      // fence that write-after-read is unordered: on L2-resident pages the
+      // refill landed first and the key was scaled by the scale of the tile
+      // four steps ahead.
+      const float scale = ptx::lds_f32_ordered(base_addr + kOffScale + 4u * (s * kTileKeys + row));
+      ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
       const int buf = i & 1;
@@ -327,16 +334,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         aborted = true;
         break;
       }
+      __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
       ptx::tc_fence_after();
-      uint32_t a[32], c[32];
-      ptx::tmem_ld_32x32b_x32(tmem + t_lane + static_cast<uint32_t>(buf * kHeads), a);
-      ptx::tmem_ld_32x32b_x32(tmem + t_lane + static_cast<uint32_t>(buf * kHeads + 32), c);
-      ptx::tmem_ld_wait();
+      uint32_t acc[64];
+      ptx::tmem_ld_32x32b_x64_sync(tmem + t_lane + static_cast<uint32_t>(buf * kHeads), acc);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
 
-      const float score = head_reduce(a, c, s_w, scale);
+      const float score = head_reduce(acc, s_w, scale);
       const int64_t pos = static_cast<int64_t>(pg_first + 2 * i) * kPage + row;
       const bool valid = pos >= key_lo && pos < key_hi;
       if (kMode == kModeScores) {

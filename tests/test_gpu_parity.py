@@ -234,3 +234,13 @@ def test_seq_len_clamped_flags_status(pkg):
     out = run(pkg, w)
     assert pkg.device_status(0) & pkg.DSA_STATUS_SEQ_CLAMPED
     assert (out[0, :1024] >= 0).all() and (out[0, 1024:] == -1).all()
+
+
+@pytest.mark.parametrize("g", [1, 2, 3, 8])
+def test_forced_cluster_sizes_l2_resident(pkg, g, monkeypatch):
+    """Every cluster size on a shared, L2-resident K (an epilogue-bound
+    pipeline where ring stages are refilled fastest): rows of 9-70 tiles per
+    CTA, so every ring stage is reused several times."""
+    monkeypatch.setenv("DSA_TOPK_CLUSTER", str(g))
+    w = workloads().make_shared("l2res", 192, 9000, 160, 21)
+    assert_parity(pkg, _rows(w, list(range(0, 192, 3))))
