@@ -90,6 +90,13 @@ DSA_API int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* cand
                            const int32_t* seq_lens, const int32_t* block_table,
                            int32_t* topk_indices, int64_t batch, int64_t max_pages, void* stream);
 
+/* Makes `device` the current CUDA device of the calling host thread for this
+ * library (the entry points above run on the current device). Callers that
+ * link their own CUDA runtime (PyTorch, TVM-FFI hosts) call it with the
+ * tensors' device before each launch. No counterpart in the reference, whose
+ * host code does the same with at::cuda::CUDAGuard (kernel.cu:826). */
+DSA_API int dsa_topk_indexer_set_device(int device);
+
 /* Reads (and optionally clears) the status word of device `device`.
  * Synchronous with respect to the device. */
 DSA_API int dsa_topk_indexer_status(int device, uint32_t* status, int clear);

@@ -39,6 +39,12 @@ def _stream(device):
     return ctypes.c_void_p(_torch().cuda.current_stream(device).cuda_stream)
 
 
+def _select(lib, device):
+    """Makes the tensors' device current for the library's CUDA runtime."""
+    _lib.check(lib.dsa_topk_indexer_set_device(int(device.index if device.index is not None else
+                                                   _torch().cuda.current_device())), "set_device")
+
+
 def _require(cond, msg):
     if not cond:
         raise RuntimeError(msg)
@@ -81,6 +87,7 @@ def launch_topk_c(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table
              and topk_indices.dtype == torch.int32 and tuple(topk_indices.shape) == (B, TOPK),
              "topk_indices must be a contiguous int32 [B, 2048] tensor on the same device")
     lib = _lib.load()
+    _select(lib, q_index_fp8.device)
     with torch.cuda.device(q_index_fp8.device):
         rc = lib.dsa_topk_indexer_launch(
             _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
@@ -98,6 +105,7 @@ def indexer_scores(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_tabl
              and scores.shape[0] == B and scores.shape[1] >= max_pages * PAGE_SIZE,
              "scores must be contiguous float32 [B, >= max_num_pages*64]")
     lib = _lib.load()
+    _select(lib, q_index_fp8.device)
     with torch.cuda.device(q_index_fp8.device):
         rc = lib.dsa_topk_indexer_scores(
             _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
@@ -120,6 +128,7 @@ def indexer_partial(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_tab
              and cand_pos.is_contiguous() and cand_pos.dtype == torch.int32 and tuple(cand_pos.shape) == (B, TOPK),
              "cand_scores / cand_pos must be contiguous [B, 2048] float32 / int32")
     lib = _lib.load()
+    _select(lib, dev)
     with torch.cuda.device(dev):
         rc = lib.dsa_topk_indexer_partial(
             _ptr(q_index_fp8), _ptr(k_index_cache_fp8), _ptr(weights), _ptr(seq_lens), _ptr(block_table),
@@ -141,6 +150,7 @@ def indexer_merge(cand_scores, cand_pos, seq_lens, block_table, topk_indices=Non
     _require(block_table.dtype == torch.int32 and block_table.shape[0] == B and block_table.is_contiguous(),
              "block_table must be contiguous int32 [B, max_num_pages]")
     lib = _lib.load()
+    _select(lib, dev)
     with torch.cuda.device(dev):
         rc = lib.dsa_topk_indexer_merge(_ptr(cand_scores.contiguous()), _ptr(cand_pos.contiguous()), nparts,
                                         _ptr(seq_lens), _ptr(block_table), _ptr(topk_indices), B,

@@ -336,6 +336,12 @@ extern "C" int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* c
   return DSA_OK;
 }
 
+extern "C" int dsa_topk_indexer_set_device(int device) {
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur == device) return DSA_OK;
+  return cudaSetDevice(device) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
 extern "C" int dsa_topk_indexer_status(int device, uint32_t* status, int clear) {
   if (!status) return DSA_ERR_INVALID_ARG;
   int prev = 0;

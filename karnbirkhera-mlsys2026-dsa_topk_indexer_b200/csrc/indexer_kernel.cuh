@@ -427,9 +427,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       hb[tid] = 0u;
       __syncthreads();
       const uint64_t hi_mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-      for (uint32_t i = tid; i < n; i += kThreads) {
-        const uint64_t key = cand[i];
-        if ((key & hi_mask) == prefix) atomicAdd(&hb[(key >> shift) & 255u], 1u);
+      for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
+        const uint32_t i = i0 + tid;
+        const uint64_t key = i < n ? cand[i] : 0ull;
+        warp_hist_add(hb, i < n && (key & hi_mask) == prefix, static_cast<uint32_t>(key >> shift) & 255u);
       }
       ptx::cluster_sync();  // every CTA's histogram of this pass is complete
       const uint32_t hb_addr = ptx::smem_addr(hb + tid);

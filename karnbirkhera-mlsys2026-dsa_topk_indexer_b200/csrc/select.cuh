@@ -45,6 +45,16 @@ __device__ __forceinline__ void group_sync() {
     ptx::named_bar(BAR, NT);
 }
 
+// Adds this lane's digit to hist (256 bins), one atomic per distinct digit in
+// the warp. Scores of one row share their high bits, so plain per-lane
+// atomics would serialise on one or two bins. All 32 lanes must call it.
+__device__ __forceinline__ void warp_hist_add(uint32_t* hist, bool active, uint32_t digit) {
+  const uint32_t d = active ? digit : 256u;
+  const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
+  const int lane = threadIdx.x & 31;
+  if (active && (__ffs(peers) - 1) == lane) atomicAdd(&hist[d], static_cast<uint32_t>(__popc(peers)));
+}
+
 // One warp scans a 256-bin histogram from the top digit down and finds the
 // digit d with count(digits > d) < krem <= count(digits >= d).
 // Writes sel = {d, count(digits > d), count(d)}.
@@ -94,9 +104,10 @@ __device__ uint64_t group_select(const uint64_t* cand, uint32_t n, uint32_t k, u
     for (int i = gt; i < 256; i += NT) hist[i] = 0u;
     group_sync<NT, BAR>();
     const uint64_t hi_mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-    for (uint32_t i = gt; i < n; i += NT) {
-      const uint64_t key = cand[i];
-      if ((key & hi_mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    for (uint32_t i0 = 0; i0 < n; i0 += NT) {
+      const uint32_t i = i0 + gt;
+      const uint64_t key = i < n ? cand[i] : 0ull;
+      warp_hist_add(hist, i < n && (key & hi_mask) == prefix, static_cast<uint32_t>(key >> shift) & 255u);
     }
     group_sync<NT, BAR>();
     if (gt < 32) find_digit_warp(hist, krem, sel);
