@@ -22,7 +22,9 @@ namespace dsa {
 // compacted to the exact best 2048 after every part.
 constexpr int kMergeThreads = 256;
 constexpr int kMergeCap = 4096;
-constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 64;
+// cand keys, histogram, misc words (count, digit scan, min/max, scan scratch),
+// then the ordering scratch (bucket counts, starts, fill).
+constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 128 + 3 * 2048 * 4;
 
 __global__ void __launch_bounds__(kMergeThreads, 1)
     merge_kernel(const float* __restrict__ cand_scores, const int32_t* __restrict__ cand_pos, int nparts,
@@ -30,7 +32,9 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
   extern __shared__ __align__(16) uint8_t msmem[];
   uint64_t* cand = reinterpret_cast<uint64_t*>(msmem);
   uint32_t* hist = reinterpret_cast<uint32_t*>(msmem + kMergeCap * 8);
-  uint32_t* misc = hist + 256;  // [0] count, [4..6] digit scan
+  uint32_t* misc = hist + 256;  // [0] count, [4..6] digit scan, [8..11] min/max, [16..23] scan scratch
+  unsigned long long* mm = reinterpret_cast<unsigned long long*>(misc + 8);
+  uint32_t* rank_cnt = misc + 32;
   const int tid = threadIdx.x, lane = tid & 31;
   const int b = blockIdx.x;
   if (tid == 0) misc[0] = 0u;
@@ -61,21 +65,31 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
     const uint32_t n = misc[0];
     __syncthreads();
     if (n > static_cast<uint32_t>(kTopK)) {
-      thr = group_select<kMergeThreads, 0>(cand, n, kTopK, hist, misc + 4, tid);
+      if (tid == 0) {
+        mm[0] = ~0ull;
+        mm[1] = 0ull;
+      }
+      __syncthreads();
+      group_minmax<kMergeThreads, 0>(cand, n, mm, tid);
+      thr = group_select<kMergeThreads, 0>(cand, n, kTopK, mm, hist, misc + 4, tid);
       group_compact<kMergeThreads, 0, kMergeCap / kMergeThreads>(cand, n, thr, misc, tid);
     }
   }
   __syncthreads();
   const uint32_t nsel = misc[0] < static_cast<uint32_t>(kTopK) ? misc[0] : static_cast<uint32_t>(kTopK);
-  for (uint32_t i = nsel + tid; i < static_cast<uint32_t>(kTopK); i += kMergeThreads) cand[i] = 0ull;
-  __syncthreads();
-  uint64_t v[8];
-  block_sort_desc_2048(cand, v);
+  RankScratch sc;
+  sc.tmp = cand + kTopK;
+  sc.cnt = rank_cnt;
+  sc.start = rank_cnt + 2048;
+  sc.fill = rank_cnt + 4096;
+  sc.wsum = misc + 16;
+  sc.mm = mm;
+  block_rank_order<0>(cand, nsel, sc);
   const int32_t* bt_row = block_table + static_cast<int64_t>(b) * max_pages;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
-    const uint32_t pos = key_pos(v[r]);
+    const uint32_t pos = i < nsel ? key_pos(cand[i]) : 0u;
     out[static_cast<int64_t>(b) * kTopK + i] =
         (i < nsel) ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
   }

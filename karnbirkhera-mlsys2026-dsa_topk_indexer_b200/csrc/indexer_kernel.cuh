@@ -3,21 +3,21 @@
 // One thread-block cluster of G CTAs serves one request (one query row).
 // The request's pages are cut into tiles of two pages (128 keys, the MMA M
 // dimension) and the tiles are split evenly over the G CTAs. Each CTA is
-// warp-specialised:
+// warp-specialised (10 warps):
 //   warp 0      TMA producer: per tile, two 8 KB page-data boxes (128-byte
 //               swizzle) and two 256 B scale rows into a 4-stage ring;
-//   warp 1      TMEM owner and MMA issuer: D[128 keys x 64 heads] (fp32, TMEM,
-//               double-buffered) = K_tile[128 x 128 e4m3] . Q[64 x 128 e4m3]^T
+//   warp 1      TMEM owner and MMA issuer: D[128 keys x 64 heads] (fp32 in
+//               TMEM, 4 buffers) = K_tile[128 x 128 e4m3] . Q[64 x 128 e4m3]^T
 //               as four tcgen05.mma kind::f8f6f4 (K = 32 each);
-//   warps 2..5  epilogue: thread = TMEM lane = key; tcgen05.ld of its 64
-//               head columns, relu / head-weight / scale reduction in
-//               registers, then a threshold filter into a shared-memory
-//               candidate buffer with periodic exact compaction to the best
-//               2048;
-//   all warps   after the stream: cluster-wide radix select of the best 2048
-//               over every CTA's candidates (histograms summed through
+//   warps 2..9  two epilogue groups of four warps (even / odd tiles): thread =
+//               TMEM lane = key; tcgen05.ld of its 64 head columns, relu /
+//               head-weight / scale reduction in registers (packed fp32x2
+//               FMA), then a threshold filter into a shared-memory candidate
+//               buffer that is cut back towards the best 2048 when it fills;
+//   all warps   after the stream: cluster-wide exact radix select of the best
+//               2048 over every CTA's candidates (histograms summed through
 //               distributed shared memory), survivors written into CTA 0's
-//               shared memory, sorted there and translated to physical slots.
+//               shared memory, ordered there and translated to physical slots.
 // Scores never go to HBM in the top-K modes.
 //
 // Reference counterparts: fp8_mma_final_scores_kernel
@@ -40,11 +40,17 @@ constexpr int kPageBytes = 8448;
 constexpr int kPageData = 8192;
 constexpr int kTileKeys = 128;
 constexpr int kStages = 4;
-constexpr int kThreads = 256;
-constexpr int kCap = 3072;  // candidate keys per CTA (>= 2048 + 128 * 8)
-constexpr int kTmemCols = 128;
+constexpr int kThreads = 320;     // 10 warps
+constexpr int kEpiThreads = 256;  // warps 2..9
+constexpr int kCap = 3072;        // candidate keys per CTA
+constexpr int kTmemBufs = 4;
+constexpr int kTmemCols = kTmemBufs * kHeads;
 
 enum Mode : int { kModeTopK = 0, kModeScores = 1, kModePartial = 2 };
+
+// Named barriers (0 is __syncthreads).
+constexpr int kBarEpi = 1;   // the 256 epilogue threads
+constexpr int kBarLow = 2;   // threads 0..255 (final ordering in CTA 0)
 
 // Shared memory map (byte offsets from a 1024-aligned base).
 constexpr int kOffK = 0;                                  // kStages x 16384, swizzled K tiles
@@ -54,13 +60,17 @@ constexpr int kOffCand = kOffScale + kStages * 512;       // kCap x 8
 constexpr int kOffHist = kOffCand + kCap * 8;             // 2 x 256 x 4
 constexpr int kOffTot = kOffHist + 2 * 256 * 4;           // 256 x 4
 constexpr int kOffW = kOffTot + 256 * 4;                  // 64 x 4
-constexpr int kOffBar = kOffW + 256;                      // (2*kStages + 5) x 8
-constexpr int kOffMisc = kOffBar + 128;                   // small words
+constexpr int kOffBar = kOffW + 256;                      // (2*kStages + 2*kTmemBufs + 1) x 8
+constexpr int kOffMisc = kOffBar + 256;                   // small words
 constexpr int kSmemUsed = kOffMisc + 128;
 constexpr int kSmemBytes = kSmemUsed + 1024;              // alignment slack
-constexpr int kOffFinal = kOffK;                          // 2048 x 8, reuses the K ring after the stream
-static_assert(kOffFinal + kTopK * 8 <= kOffQ, "final buffer must fit in the K ring");
+// After the stream the K ring is free: CTA 0 orders the survivors there.
+constexpr int kOffFinal = kOffK;                          // 2048 x 8
+constexpr int kOffRankTmp = kOffFinal + kTopK * 8;        // 2048 x 8
+constexpr int kOffRankCnt = kOffRankTmp + kTopK * 8;      // 3 x 2048 x 4 (cnt, start, fill)
+static_assert(kOffRankCnt + 3 * 2048 * 4 <= kOffQ, "ordering scratch must fit in the K ring");
 static_assert(kStages * 16384 % 1024 == 0, "K tiles must stay 1024-aligned");
+static_assert((2 * kStages + 2 * kTmemBufs + 1) * 8 <= 256, "barrier area");
 
 // Misc word indices (uint32 at kOffMisc).
 enum MiscWord : int {
@@ -72,6 +82,9 @@ enum MiscWord : int {
   kMiscTotal = 10,
   kMiscOffset = 11,
   kMiscWrite = 12,
+  kMiscMM = 16,     // 2 x u64: min / max of the local candidates
+  kMiscPubMM = 20,  // 2 x u64 read by other CTAs of the cluster
+  kMiscWsum = 24,   // 8 words: scan scratch of the final ordering
 };
 
 struct IndexerParams {
@@ -91,49 +104,38 @@ struct IndexerParams {
 
 __device__ unsigned int g_dsa_status;
 
-// score = sum_h w_h * relu(scale * acc_h), evaluated as
-// |scale| * sum_h w_h * relu(sign(scale) * acc_h): the scale is applied once
-// per key instead of once per head (exact up to fp32 rounding, any sign).
-__device__ __forceinline__ float head_reduce(const uint32_t (&acc)[64], const float* s_w,
-                                             float scale) {
-  const float4* w4 = reinterpret_cast<const float4*>(s_w);
-  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-  if (scale >= 0.f) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 w = w4[j];
-      s0 = fmaf(w.x, fmaxf(__uint_as_float(acc[4 * j + 0]), 0.f), s0);
-      s1 = fmaf(w.y, fmaxf(__uint_as_float(acc[4 * j + 1]), 0.f), s1);
-      s2 = fmaf(w.z, fmaxf(__uint_as_float(acc[4 * j + 2]), 0.f), s2);
-      s3 = fmaf(w.w, fmaxf(__uint_as_float(acc[4 * j + 3]), 0.f), s3);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 w = w4[8 + j];
-      s0 = fmaf(w.x, fmaxf(__uint_as_float(acc[32 + 4 * j + 0]), 0.f), s0);
-      s1 = fmaf(w.y, fmaxf(__uint_as_float(acc[32 + 4 * j + 1]), 0.f), s1);
-      s2 = fmaf(w.z, fmaxf(__uint_as_float(acc[32 + 4 * j + 2]), 0.f), s2);
-      s3 = fmaf(w.w, fmaxf(__uint_as_float(acc[32 + 4 * j + 3]), 0.f), s3);
-    }
-    return ((s0 + s1) + (s2 + s3)) * scale;
-  }
+// d0 += a0 * b0 and d1 += a1 * b1 in one packed fp32x2 FMA.
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// acc[h] for 32 heads [h0, h0+32): s[] += w_h * relu(sgn * acc_h), eight
+// independent accumulators. The per-key scale is applied by the caller once
+// to the sum: relu(scale * x) = |scale| * relu(sign(scale) * x).
+template <bool kNeg>
+__device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], const float* s_w, int h0,
+                                                 float (&s)[8]) {
+  const float4* w4 = reinterpret_cast<const float4*>(s_w + h0);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 w = w4[j];
-    s0 = fmaf(w.x, fmaxf(-__uint_as_float(acc[4 * j + 0]), 0.f), s0);
-    s1 = fmaf(w.y, fmaxf(-__uint_as_float(acc[4 * j + 1]), 0.f), s1);
-    s2 = fmaf(w.z, fmaxf(-__uint_as_float(acc[4 * j + 2]), 0.f), s2);
-    s3 = fmaf(w.w, fmaxf(-__uint_as_float(acc[4 * j + 3]), 0.f), s3);
-  }
+    float r[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float4 w = w4[8 + j];
-    s0 = fmaf(w.x, fmaxf(-__uint_as_float(acc[32 + 4 * j + 0]), 0.f), s0);
-    s1 = fmaf(w.y, fmaxf(-__uint_as_float(acc[32 + 4 * j + 1]), 0.f), s1);
-    s2 = fmaf(w.z, fmaxf(-__uint_as_float(acc[32 + 4 * j + 2]), 0.f), s2);
-    s3 = fmaf(w.w, fmaxf(-__uint_as_float(acc[32 + 4 * j + 3]), 0.f), s3);
+    for (int e = 0; e < 4; ++e) {
+      const float v = __uint_as_float(acc[4 * j + e]);
+      r[e] = fmaxf(kNeg ? -v : v, 0.f);
+    }
+    const int a = (j & 1) * 4;
+    ffma2(s[a + 0], s[a + 1], w.x, w.y, r[0], r[1]);
+    ffma2(s[a + 2], s[a + 3], w.z, w.w, r[2], r[3]);
   }
-  return ((s0 + s1) + (s2 + s3)) * (-scale);
 }
 
 template <int kMode>
@@ -152,12 +154,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc);
   uint32_t* misc_nv = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = misc + kMiscAbort;
+  unsigned long long* mm = reinterpret_cast<unsigned long long*>(smem + kOffMisc + 4 * kMiscMM);
+  unsigned long long* pub_mm = reinterpret_cast<unsigned long long*>(smem + kOffMisc + 4 * kMiscPubMM);
 
-  const uint32_t bar_full = base_addr + kOffBar;              // [kStages]
-  const uint32_t bar_empty = bar_full + 8 * kStages;          // [kStages]
-  const uint32_t bar_tfull = bar_empty + 8 * kStages;         // [2]
-  const uint32_t bar_tempty = bar_tfull + 16;                 // [2]
-  const uint32_t bar_q = bar_tempty + 16;                     // [1]
+  const uint32_t bar_full = base_addr + kOffBar;                // [kStages]
+  const uint32_t bar_empty = bar_full + 8 * kStages;            // [kStages]
+  const uint32_t bar_tfull = bar_empty + 8 * kStages;           // [kTmemBufs]
+  const uint32_t bar_tempty = bar_tfull + 8 * kTmemBufs;        // [kTmemBufs]
+  const uint32_t bar_q = bar_tempty + 8 * kTmemBufs;            // [1]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -193,9 +197,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, 1 + 4);  // MMA commit + 4 epilogue warps (scales read)
+      ptx::mbar_init(bar_empty + 8 * s, 1 + 4);  // MMA commit + the 4 warps of one epilogue group
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTmemBufs; ++i) {
       ptx::mbar_init(bar_tfull + 8 * i, 1);
       ptx::mbar_init(bar_tempty + 8 * i, 4);
     }
@@ -219,8 +223,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   ptx::tc_fence_after();
   const uint32_t tmem = misc_nv[kMiscTmem];
 
-  int issued = 0;       // producer: tiles whose loads were issued
-  int mma_issued = 0;   // MMA warp: tiles whose MMAs were issued
+  int issued = 0;      // producer: tiles whose loads were issued
+  int mma_issued = 0;  // MMA warp: tiles whose MMAs were issued
   bool aborted = false;
 
   if (warp == 0) {
@@ -277,8 +281,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < my_tiles && !aborted; ++i) {
       const int s = i % kStages;
       const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-      const int buf = i & 1;
-      const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
+      const int buf = i % kTmemBufs;
+      const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
       ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT) &&
            ptx::mbar_wait(bar_tempty + 8 * buf, bph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
       if (__any_sync(0xFFFFFFFFu, !ok)) {
@@ -299,17 +303,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       mma_issued = i + 1;
     }
-  } else if (warp < 6) {
-    // ===================== epilogue =====================
-    const int q4 = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = q4 * 32 + lane;     // key row inside the 128-key tile
-    const int et = threadIdx.x - 64;    // 0..127 inside the epilogue group
+  } else {
+    // ===================== epilogue: two groups of four warps =====================
+    // Group 0 (warps 2-5) takes the even tiles, group 1 (warps 6-9) the odd
+    // ones, so two tiles are reduced at once. Within a group, warp w reads
+    // TMEM lane quarter w % 4, i.e. thread = key row of the tile.
+    const int grp = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int et = threadIdx.x - 64;  // 0..255 over both groups
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
-    uint64_t thr = 0;                   // keys below thr can no longer reach the top 2048
+    const int n_pairs_full = my_tiles >> 1;
+    uint64_t thr = 0;  // keys below thr can no longer reach the top 2048
     int since = 0;
-    int check_every = kCap / kTileKeys;
+    int check_every = kCap / (2 * kTileKeys);
 #pragma unroll 1
-    for (int i = 0; i < my_tiles; ++i) {
+    for (int i = grp; i < my_tiles; i += 2) {
       const int s = i % kStages;
       const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
       bool ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
@@ -319,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // The scale is read with a generic-proxy load, and the producer's next
       // TMA into this stage writes through the async proxy as soon as the MMA
-      // commit and all four epilogue warps have arrived. Without the proxy
+      // commit and this group's four warps have arrived. Without the proxy
       // fence that write-after-read is unordered: on L2-resident pages the
       // refill landed first and the key was scaled by the scale of the tile
       // four steps ahead.
@@ -327,8 +336,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
-      const int buf = i & 1;
-      const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
+      const int buf = i % kTmemBufs;
+      const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
       ok = ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
       if (__any_sync(0xFFFFFFFFu, !ok)) {
         aborted = true;
@@ -336,13 +345,28 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
       ptx::tc_fence_after();
-      uint32_t acc[64];
-      ptx::tmem_ld_32x32b_x64_sync(tmem + t_lane + static_cast<uint32_t>(buf * kHeads), acc);
+      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      {
+        uint32_t acc[32];
+        const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(buf * kHeads);
+        ptx::tmem_ld_32x32b_x32_sync(ta, acc);
+        if (scale >= 0.f)
+          head_reduce_half<false>(acc, s_w, 0, sums);
+        else
+          head_reduce_half<true>(acc, s_w, 0, sums);
+        ptx::tmem_ld_32x32b_x32_sync(ta + 32u, acc);
+        if (scale >= 0.f)
+          head_reduce_half<false>(acc, s_w, 32, sums);
+        else
+          head_reduce_half<true>(acc, s_w, 32, sums);
+      }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
 
-      const float score = head_reduce(acc, s_w, scale);
+      const float score =
+          (((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]))) *
+          fabsf(scale);
       const int64_t pos = static_cast<int64_t>(pg_first + 2 * i) * kPage + row;
       const bool valid = pos >= key_lo && pos < key_hi;
       if (kMode == kModeScores) {
@@ -358,20 +382,34 @@ __global__ void __launch_bounds__(kThreads, 2)
           base = __shfl_sync(0xFFFFFFFFu, base, leader);
           if (keep) cand[base + __popc(m & lanemask_lt())] = key;
         }
-        // Every check_every tiles the buffer may be full: compact it to the
-        // exact best 2048 and raise the threshold. The schedule depends only
-        // on tile counts, so all four warps take the same barriers.
+        // After every check_every tile pairs the buffer may be nearly full:
+        // both groups meet and cut it back. The schedule depends only on tile
+        // counts, so all eight warps take the same barriers.
         if (++since == check_every) {
-          ptx::named_bar(1, 128);
-          uint32_t n = misc[kMiscCount];
-          ptx::named_bar(1, 128);
-          if (n > static_cast<uint32_t>(kTopK)) {
-            thr = group_select<128, 1>(cand, n, kTopK, hist, misc_nv + kMiscSel, et);
-            group_compact<128, 1, kCap / 128>(cand, n, thr, misc_nv + kMiscCount, et);
-            n = kTopK;
-          }
           since = 0;
-          check_every = static_cast<int>((kCap - n) / kTileKeys);
+          if ((i >> 1) < n_pairs_full) {
+            ptx::named_bar(kBarEpi, kEpiThreads);
+            uint32_t n = misc[kMiscCount];
+            if (et == 0) {
+              mm[0] = ~0ull;
+              mm[1] = 0ull;
+            }
+            ptx::named_bar(kBarEpi, kEpiThreads);
+            if (n > static_cast<uint32_t>(kTopK)) {
+              // Cheap safe cut; the exact selection only if the cut frees
+              // too little room. Keys below the cut can never reach the top
+              // 2048.
+              group_minmax<kEpiThreads, kBarEpi>(cand, n, mm, et);
+              uint32_t kept = 0;
+              uint64_t T = group_cut<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, &kept);
+              if (kept > static_cast<uint32_t>(kCap - 4 * kTileKeys))
+                T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
+              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, et);
+              thr = T;
+              n = misc[kMiscCount];
+            }
+            check_every = static_cast<int>((kCap - n) / (2 * kTileKeys));
+          }
         }
       }
     }
@@ -391,8 +429,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     if (warp == 1 && lane == 0 && mma_issued > 0) {
       const int last = mma_issued - 1;
-      ptx::mbar_wait(bar_tfull + 8 * (last & 1), static_cast<uint32_t>(last >> 1) & 1u, &no_abort,
-                     &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+      ptx::mbar_wait(bar_tfull + 8 * (last % kTmemBufs), static_cast<uint32_t>(last / kTmemBufs) & 1u,
+                     &no_abort, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
     }
     __syncthreads();
   }
@@ -406,46 +444,69 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x;
   const uint32_t n = misc_nv[kMiscCount];
   const uint32_t pub_addr = base_addr + kOffMisc + 4 * kMiscPub;
-  if (tid == 0) misc_nv[kMiscPub] = n;
+  const uint32_t pub_mm_addr = base_addr + kOffMisc + 4 * kMiscPubMM;
+  if (tid == 0) {
+    mm[0] = ~0ull;
+    mm[1] = 0ull;
+  }
+  __syncthreads();
+  group_minmax<kThreads, 0>(cand, n, mm, tid);
+  if (tid == 0) {
+    misc_nv[kMiscPub] = n;
+    pub_mm[0] = mm[0];
+    pub_mm[1] = mm[1];
+  }
   ptx::cluster_sync();
   if (warp == 0) {
-    uint32_t v = (static_cast<uint32_t>(lane) < G) ? ptx::ld_dsmem_u32(ptx::mapa(pub_addr, lane)) : 0u;
+    // Cluster totals: candidate count, smallest and largest key.
+    uint32_t v = 0;
+    unsigned long long lo = ~0ull, hi = 0ull;
+    if (static_cast<uint32_t>(lane) < G) {
+      v = ptx::ld_dsmem_u32(ptx::mapa(pub_addr, lane));
+      const uint32_t a = ptx::mapa(pub_mm_addr, lane);
+      lo = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 4)) << 32) | ptx::ld_dsmem_u32(a);
+      hi = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 12)) << 32) | ptx::ld_dsmem_u32(a + 8);
+    }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-    if (lane == 0) misc_nv[kMiscTotal] = v;
+    for (int off = 16; off > 0; off >>= 1) {
+      v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+      const unsigned long long x = __shfl_xor_sync(0xFFFFFFFFu, lo, off);
+      const unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, hi, off);
+      lo = x < lo ? x : lo;
+      hi = y > hi ? y : hi;
+    }
+    if (lane == 0) {
+      misc_nv[kMiscTotal] = v;
+      mm[0] = lo;
+      mm[1] = hi;
+    }
   }
   __syncthreads();
   const uint32_t total = misc_nv[kMiscTotal];
   uint64_t T = 0;
   if (total > static_cast<uint32_t>(kTopK)) {
-    uint64_t prefix = 0;
-    uint32_t krem = kTopK;
+    RadixState st = radix_start(mm[0], mm[1], kTopK);
     int pass = 0;
 #pragma unroll 1
-    for (int shift = 56; shift >= 0; shift -= 8, ++pass) {
+    while (true) {
       uint32_t* hb = hist + (pass & 1) * 256;
-      hb[tid] = 0u;
+      if (tid < 256) hb[tid] = 0u;
       __syncthreads();
-      const uint64_t hi_mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-      for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
-        const uint32_t i = i0 + tid;
-        const uint64_t key = i < n ? cand[i] : 0ull;
-        warp_hist_add(hb, i < n && (key & hi_mask) == prefix, static_cast<uint32_t>(key >> shift) & 255u);
-      }
+      radix_hist<kThreads>(cand, n, st, hb, tid);
       ptx::cluster_sync();  // every CTA's histogram of this pass is complete
-      const uint32_t hb_addr = ptx::smem_addr(hb + tid);
-      uint32_t sum = 0;
-      for (uint32_t r = 0; r < G; ++r) sum += ptx::ld_dsmem_u32(ptx::mapa(hb_addr, r));
-      tot[tid] = sum;
+      if (tid < 256) {
+        const uint32_t hb_addr = ptx::smem_addr(hb + tid);
+        uint32_t sum = 0;
+        for (uint32_t r = 0; r < G; ++r) sum += ptx::ld_dsmem_u32(ptx::mapa(hb_addr, r));
+        tot[tid] = sum;
+      }
       __syncthreads();
-      if (warp == 0) find_digit_warp(tot, krem, misc_nv + kMiscSel);
+      if (warp == 0) find_digit_warp(tot, st.krem, misc_nv + kMiscSel);
       __syncthreads();
-      const uint32_t d = misc_nv[kMiscSel], cgt = misc_nv[kMiscSel + 1], cd = misc_nv[kMiscSel + 2];
-      prefix |= static_cast<uint64_t>(d) << shift;
-      krem -= cgt;
-      if (cd == krem) break;
+      if (radix_advance(st, misc_nv + kMiscSel)) break;
+      ++pass;
     }
-    T = prefix;
+    T = st.prefix;
   }
   // Count this CTA's survivors, publish, and get this CTA's output offset.
   {
@@ -481,27 +542,31 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (keep) ptx::st_dsmem_u64(fin_remote + 8u * (my_off + base + __popc(m & lanemask_lt())), key);
       }
     }
-    if (rank == 0) {
-      uint64_t* fin = reinterpret_cast<uint64_t*>(smem + kOffFinal);
-      for (uint32_t i = nsel + tid; i < static_cast<uint32_t>(kTopK); i += kThreads) fin[i] = 0ull;
-    }
   }
   ptx::cluster_sync();
-  if (rank != 0) return;
+  if (rank != 0 || tid >= 256) return;
 
-  // ---- CTA 0: sort the survivors and emit ----
-  uint64_t v[8];
-  block_sort_desc_2048(reinterpret_cast<uint64_t*>(smem + kOffFinal), v);
+  // ---- CTA 0, threads 0..255: order the survivors and emit ----
+  uint64_t* fin = reinterpret_cast<uint64_t*>(smem + kOffFinal);
+  RankScratch sc;
+  sc.tmp = reinterpret_cast<uint64_t*>(smem + kOffRankTmp);
+  sc.cnt = reinterpret_cast<uint32_t*>(smem + kOffRankCnt);
+  sc.start = sc.cnt + 2048;
+  sc.fill = sc.start + 2048;
+  sc.wsum = misc_nv + kMiscWsum;
+  sc.mm = mm;
+  block_rank_order<kBarLow>(fin, nsel, sc);
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
     const bool live = i < nsel;
-    const uint32_t pos = key_pos(v[r]);
+    const uint64_t key = live ? fin[i] : 0ull;
+    const uint32_t pos = key_pos(key);
     const int64_t o = static_cast<int64_t>(b) * kTopK + i;
     if (kMode == kModeTopK) {
       p.out[o] = live ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
     } else {
-      p.cand_scores[o] = live ? ordered_to_float(static_cast<uint32_t>(v[r] >> 32)) : -__int_as_float(0x7f800000);
+      p.cand_scores[o] = live ? ordered_to_float(static_cast<uint32_t>(key >> 32)) : -__int_as_float(0x7f800000);
       p.cand_pos[o] = live ? static_cast<int32_t>(pos) : -1;
     }
   }

@@ -45,14 +45,29 @@ __device__ __forceinline__ void group_sync() {
     ptx::named_bar(BAR, NT);
 }
 
-// Adds this lane's digit to hist (256 bins), one atomic per distinct digit in
-// the warp. Scores of one row share their high bits, so plain per-lane
-// atomics would serialise on one or two bins. All 32 lanes must call it.
-__device__ __forceinline__ void warp_hist_add(uint32_t* hist, bool active, uint32_t digit) {
-  const uint32_t d = active ? digit : 256u;
-  const uint32_t peers = __match_any_sync(0xFFFFFFFFu, d);
-  const int lane = threadIdx.x & 31;
-  if (active && (__ffs(peers) - 1) == lane) atomicAdd(&hist[d], static_cast<uint32_t>(__popc(peers)));
+// Radix-select state: the top `top` bits of the sought key are known and
+// equal `prefix` (lower bits zero); krem keys are still to be taken from the
+// keys that share that prefix.
+struct RadixState {
+  uint64_t prefix;
+  int top;
+  uint32_t krem;
+};
+
+__device__ __forceinline__ uint64_t high_mask(int top) { return top <= 0 ? 0ull : (~0ull << (64 - top)); }
+
+// Next digit window below the known prefix: [shift, shift + width).
+__device__ __forceinline__ int window_width(int top) { return (64 - top) < 8 ? (64 - top) : 8; }
+
+// Start state for selecting among keys in [lo, hi]: their common leading bits
+// are already known, so the first pass looks at the first bits that differ.
+__device__ __forceinline__ RadixState radix_start(uint64_t lo, uint64_t hi, uint32_t k) {
+  RadixState st;
+  const uint64_t x = lo ^ hi;
+  st.top = x ? __clzll(static_cast<long long>(x)) : 64;
+  st.prefix = lo & high_mask(st.top);
+  st.krem = k;
+  return st;
 }
 
 // One warp scans a 256-bin histogram from the top digit down and finds the
@@ -89,35 +104,93 @@ __device__ __forceinline__ void find_digit_warp(const uint32_t* hist, uint32_t k
   }
 }
 
-// Radix select over keys cand[0..n) held in shared memory by a group of NT
-// threads (gt = thread index in the group, warp 0 of the group does the
-// digit scan). Precondition: n > k, group synchronised. Returns T such that
-// exactly k keys are >= T. Eight passes of 8 bits at most; stops as soon as
-// the boundary bucket is taken whole.
+// Min and max of cand[0..n) over a group (results in mm[0], mm[1]; mm must be
+// preset to {~0, 0} before the group barrier that precedes the call).
 template <int NT, int BAR>
-__device__ uint64_t group_select(const uint64_t* cand, uint32_t n, uint32_t k, uint32_t* hist, uint32_t* sel,
-                                 int gt) {
-  uint64_t prefix = 0;
-  uint32_t krem = k;
+__device__ void group_minmax(const uint64_t* cand, uint32_t n, unsigned long long* mm, int gt) {
+  unsigned long long lo = ~0ull, hi = 0ull;
+  for (uint32_t i = gt; i < n; i += NT) {
+    const unsigned long long k = cand[i];
+    lo = k < lo ? k : lo;
+    hi = k > hi ? k : hi;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const unsigned long long a = __shfl_xor_sync(0xFFFFFFFFu, lo, off);
+    const unsigned long long b = __shfl_xor_sync(0xFFFFFFFFu, hi, off);
+    lo = a < lo ? a : lo;
+    hi = b > hi ? b : hi;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(&mm[0], lo);
+    atomicMax(&mm[1], hi);
+  }
+  group_sync<NT, BAR>();
+}
+
+// One histogram pass of the radix select over cand[0..n) (plain per-lane
+// atomics: below the common prefix the digits are spread out).
+template <int NT>
+__device__ __forceinline__ void radix_hist(const uint64_t* cand, uint32_t n, const RadixState& st, uint32_t* hist,
+                                           int gt) {
+  const int width = window_width(st.top);
+  const int shift = 64 - st.top - width;
+  const uint64_t hm = high_mask(st.top);
+  const uint32_t dmask = (1u << width) - 1u;
+  for (uint32_t i = gt; i < n; i += NT) {
+    const uint64_t key = cand[i];
+    if ((key & hm) == st.prefix) atomicAdd(&hist[static_cast<uint32_t>(key >> shift) & dmask], 1u);
+  }
+}
+
+// Applies the digit scan result of one pass. Returns true when done.
+__device__ __forceinline__ bool radix_advance(RadixState& st, const uint32_t* sel) {
+  const int width = window_width(st.top);
+  const int shift = 64 - st.top - width;
+  st.prefix |= static_cast<uint64_t>(sel[0]) << shift;
+  st.top += width;
+  st.krem -= sel[1];
+  return sel[2] == st.krem || st.top >= 64;
+}
+
+// Exact radix select over keys cand[0..n) held in shared memory by a group of
+// NT threads (gt = thread index in the group; warp 0 of the group scans).
+// Precondition: n > k, group synchronised, mm = {min, max} of the keys.
+// Returns T such that exactly k keys are >= T.
+template <int NT, int BAR>
+__device__ uint64_t group_select(const uint64_t* cand, uint32_t n, uint32_t k, const unsigned long long* mm,
+                                 uint32_t* hist, uint32_t* sel, int gt) {
+  RadixState st = radix_start(mm[0], mm[1], k);
 #pragma unroll 1
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  while (true) {
     for (int i = gt; i < 256; i += NT) hist[i] = 0u;
     group_sync<NT, BAR>();
-    const uint64_t hi_mask = (shift == 56) ? 0ull : (~0ull << (shift + 8));
-    for (uint32_t i0 = 0; i0 < n; i0 += NT) {
-      const uint32_t i = i0 + gt;
-      const uint64_t key = i < n ? cand[i] : 0ull;
-      warp_hist_add(hist, i < n && (key & hi_mask) == prefix, static_cast<uint32_t>(key >> shift) & 255u);
-    }
+    radix_hist<NT>(cand, n, st, hist, gt);
     group_sync<NT, BAR>();
-    if (gt < 32) find_digit_warp(hist, krem, sel);
+    if (gt < 32) find_digit_warp(hist, st.krem, sel);
     group_sync<NT, BAR>();
-    const uint32_t d = sel[0], cgt = sel[1], cd = sel[2];
-    prefix |= static_cast<uint64_t>(d) << shift;
-    krem -= cgt;
-    if (cd == krem) break;
+    if (radix_advance(st, sel)) break;
   }
-  return prefix;
+  return st.prefix;
+}
+
+// Cheap safe cut for a filling buffer: one 8-bit window just below the keys'
+// common prefix; keeps every key whose digit is >= the digit holding the
+// k-th largest key. At least k keys survive (so no key of the final top k is
+// dropped); *kept returns how many. Precondition as for group_select.
+template <int NT, int BAR>
+__device__ uint64_t group_cut(const uint64_t* cand, uint32_t n, uint32_t k, const unsigned long long* mm,
+                              uint32_t* hist, uint32_t* sel, int gt, uint32_t* kept) {
+  RadixState st = radix_start(mm[0], mm[1], k);
+  for (int i = gt; i < 256; i += NT) hist[i] = 0u;
+  group_sync<NT, BAR>();
+  radix_hist<NT>(cand, n, st, hist, gt);
+  group_sync<NT, BAR>();
+  if (gt < 32) find_digit_warp(hist, st.krem, sel);
+  group_sync<NT, BAR>();
+  *kept = sel[1] + sel[2];
+  const int width = window_width(st.top);
+  return st.prefix | (static_cast<uint64_t>(sel[0]) << (64 - st.top - width));
 }
 
 // Keeps the keys >= T of cand[0..n) and packs them to the front; `counter`
@@ -149,65 +222,87 @@ __device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* 
   group_sync<NT, BAR>();
 }
 
-// Sorts buf[0..2048) descending. 256 threads; thread t owns elements
-// [8t, 8t+8). Bitonic network: partner distances 1..4 inside a thread,
-// 8..128 across lanes of a warp (shuffles), 256..1024 through shared memory.
-__device__ __forceinline__ void cmpx(uint64_t& a, uint64_t& b, bool desc) {
-  const bool sw = desc ? (a < b) : (a > b);
-  const uint64_t x = sw ? b : a, y = sw ? a : b;
-  a = x;
-  b = y;
-}
+// Shared-memory scratch of block_rank_order (all arrays 2048 long).
+struct RankScratch {
+  uint64_t* tmp;
+  uint32_t* cnt;
+  uint32_t* start;
+  uint32_t* fill;
+  uint32_t* wsum;           // 8 words
+  unsigned long long* mm;   // 2 words
+};
 
-__device__ void block_sort_desc_2048(uint64_t* buf, uint64_t (&v)[8]) {
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int r = 0; r < 8; ++r) v[r] = buf[t * 8 + r];
-#pragma unroll
-  for (int k = 2; k <= 2048; k <<= 1) {
-    if (k >= 512) {
-      __syncthreads();
-#pragma unroll
-      for (int r = 0; r < 8; ++r) buf[t * 8 + r] = v[r];
-      __syncthreads();
-#pragma unroll
-      for (int j = k >> 1; j >= 256; j >>= 1) {
-        const int lj = __ffs(j) - 1;
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int p = t + 256 * m;
-          const int i = ((p >> lj) << (lj + 1)) | (p & (j - 1));
-          const int l = i | j;
-          uint64_t a = buf[i], c = buf[l];
-          cmpx(a, c, (i & k) == 0);
-          buf[i] = a;
-          buf[l] = c;
-        }
-        __syncthreads();
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = buf[t * 8 + r];
-    }
-#pragma unroll
-    for (int j = ((k >> 1) < 128 ? (k >> 1) : 128); j >= 1; j >>= 1) {
-      if (j >= 8) {
-        const int lx = j >> 3;
-        const bool lower = ((t & lx) == 0);
-        const bool desc = ((t * 8) & k) == 0;
-        const bool keep_max = (lower == desc);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const uint64_t p = __shfl_xor_sync(0xFFFFFFFFu, v[r], lx);
-          v[r] = keep_max ? (v[r] > p ? v[r] : p) : (v[r] < p ? v[r] : p);
-        }
-      } else {
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          if ((r & j) == 0) cmpx(v[r], v[r | j], ((t * 8 + r) & k) == 0);
-        }
-      }
-    }
+// Puts the n <= 2048 unique keys of keys[] in descending order, in place.
+// 256 threads (t = 0..255) synchronised by barrier BAR. Instead of a sorting
+// network (which on 256 threads is bound by shared-memory traffic or shuffle
+// latency at tens of thousands of cycles for 2048 64-bit keys), keys are
+// counted into 2048 buckets on the 11 bits just below their common prefix,
+// scattered bucket by bucket, and each key's final rank is the number of
+// keys in higher buckets plus the number of larger keys in its own bucket.
+// Exact for any input; a bucket holds a handful of keys for continuous
+// scores and the cost only grows when very many keys share their top bits.
+template <int BAR>
+__device__ __noinline__ void block_rank_order(uint64_t* keys, uint32_t n, const RankScratch sc) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  if (t == 0) {
+    sc.mm[0] = ~0ull;
+    sc.mm[1] = 0ull;
   }
+  for (int i = t; i < 2048; i += 256) {
+    sc.cnt[i] = 0u;
+    sc.fill[i] = 0u;
+  }
+  group_sync<256, BAR>();
+  group_minmax<256, BAR>(keys, n, sc.mm, t);
+  const uint64_t x = sc.mm[0] ^ sc.mm[1];
+  const int top = x ? __clzll(static_cast<long long>(x)) : 64;
+  const int shift = (64 - top - 11) > 0 ? (64 - top - 11) : 0;
+  for (uint32_t i = t; i < n; i += 256) atomicAdd(&sc.cnt[static_cast<uint32_t>(keys[i] >> shift) & 2047u], 1u);
+  group_sync<256, BAR>();
+  // Exclusive scan in descending bucket order; thread t owns buckets
+  // 2047-8t down to 2040-8t.
+  uint32_t c[8], tot = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = sc.cnt[2047 - 8 * t - j];
+    tot += c[j];
+  }
+  uint32_t incl = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) sc.wsum[w] = incl;
+  group_sync<256, BAR>();
+  uint32_t base = incl - tot;
+  for (int k = 0; k < w; ++k) base += sc.wsum[k];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sc.start[2047 - 8 * t - j] = base;
+    base += c[j];
+  }
+  group_sync<256, BAR>();
+  for (uint32_t i = t; i < n; i += 256) {
+    const uint64_t k = keys[i];
+    const uint32_t d = static_cast<uint32_t>(k >> shift) & 2047u;
+    sc.tmp[sc.start[d] + atomicAdd(&sc.fill[d], 1u)] = k;
+  }
+  group_sync<256, BAR>();
+  for (uint32_t i = t; i < n; i += 256) {
+    const uint64_t k = sc.tmp[i];
+    const uint32_t d = static_cast<uint32_t>(k >> shift) & 2047u;
+    const uint32_t b0 = sc.start[d], b1 = b0 + sc.cnt[d];
+    uint32_t r0 = 0, r1 = 0;
+    uint32_t q = b0;
+    for (; q + 1 < b1; q += 2) {
+      r0 += (sc.tmp[q] > k) ? 1u : 0u;
+      r1 += (sc.tmp[q + 1] > k) ? 1u : 0u;
+    }
+    if (q < b1) r0 += (sc.tmp[q] > k) ? 1u : 0u;
+    keys[b0 + r0 + r1] = k;
+  }
+  group_sync<256, BAR>();
 }
 
 }  // namespace dsa
