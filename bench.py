@@ -160,17 +160,22 @@ def main():
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    for _ in range(args.warmup):
-        flush.zero_()
-        call()
+    # Warm-up runs on the stream the step is later captured on: the library
+    # creates its per-stream workspace on the first call, outside capture.
+    cap_stream = torch.cuda.Stream(dev)
+    cap_stream.wait_stream(stream)
+    with torch.cuda.stream(cap_stream):
+        for _ in range(args.warmup):
+            flush.zero_()
+            call()
     torch.cuda.synchronize()
     pkg.device_status(local, clear=True)
 
     # The step is captured once into a CUDA graph, so the device-timed region
-    # measures the kernel, not Python launch overhead (the e2e region below
+    # measures the kernels, not Python launch overhead (the e2e region below
     # keeps direct calls).
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    with torch.cuda.graph(graph, stream=cap_stream):
         per_step = call()
     torch.cuda.synchronize()
 

@@ -8,7 +8,10 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "dsa_topk_indexer.h"
 #include "indexer_kernel.cuh"
@@ -161,6 +164,39 @@ int prepare_device(int* num_sms) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Library-owned device workspace, one per (device, stream): calls on one
+// stream are ordered, so its contents are never shared by work in flight on
+// two streams. Allocated outside stream capture the first time a launch
+// needs it and grown (never shrunk) on demand; replaced buffers are kept
+// until exit because work queued earlier may still read them.
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
+std::vector<void*> g_retired;
+std::mutex g_ws_mutex;
+
+// Returns the workspace of (current device, stream) with at least `bytes`, or
+// null if it would have to be allocated while the stream is being captured.
+void* workspace(cudaStream_t stream, size_t bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  Workspace& ws = g_workspaces[{dev, stream}];
+  if (ws.bytes >= bytes) return ws.ptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  size_t want = bytes < (1u << 16) ? (1u << 16) : bytes;
+  if (want < 2 * ws.bytes) want = 2 * ws.bytes;
+  void* fresh = nullptr;
+  if (cudaMalloc(&fresh, want) != cudaSuccess) return nullptr;
+  if (ws.ptr) g_retired.push_back(ws.ptr);
+  ws.ptr = fresh;
+  ws.bytes = want;
+  return ws.ptr;
+}
+
 // Tensor maps over the caller's buffers (encoded per call: they hold the
 // base address).
 int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_pages, CUtensorMap* tk,
@@ -203,9 +239,11 @@ int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_page
   return DSA_OK;
 }
 
-// CTAs per request (the cluster size). The longest row gets about 32 tiles
-// (4096 keys) per CTA; small batches are spread wider so the grid covers the
-// GPU, but not below about 4 tiles per CTA.
+// CTAs per request (the cluster size). Enough CTAs to give the GPU about four
+// per SM in total, so short batches split their rows widely (latency) while
+// large batches keep whole rows on few CTAs (less merging per byte); never
+// fewer than about 4 tiles per CTA. Measured on B200: B=64 -> 8 (best of
+// 2/4/8), B=512 -> 2 (best of 1/2/4/8).
 int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
   // DSA_TOPK_CLUSTER=<1..8> overrides the choice (tuning and tests).
   if (const char* env = std::getenv("DSA_TOPK_CLUSTER")) {
@@ -213,11 +251,9 @@ int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
     if (g >= 1 && g <= 8) return g;
   }
   const int64_t tiles = (span_pages + 1) / 2;
-  const int64_t g_len = (tiles + 31) / 32;
-  const int64_t g_fill = (2 * num_sms + batch - 1) / batch;
+  int64_t g = (4 * static_cast<int64_t>(num_sms) + batch - 1) / batch;
   const int64_t g_floor = (tiles + 3) / 4;
-  int64_t g = g_fill < g_floor ? g_fill : g_floor;
-  if (g_len > g) g = g_len;
+  if (g > g_floor) g = g_floor;
   if (g < 1) g = 1;
   if (g > 8) g = 8;
   return static_cast<int>(g);
@@ -244,6 +280,19 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   rc = make_maps(q, kcache, prm.batch, prm.num_pages, &tk, &ts, &tq);
   if (rc != DSA_OK) return rc;
   const int G = choose_cluster(prm.batch, span_pages, num_sms);
+  IndexerParams params = prm;
+  int launches = 1;
+  // More clusters than fit at once: serve the longest rows first so that no
+  // long row starts in the last wave.
+  if (prm.batch > 1 && static_cast<int64_t>(G) * prm.batch > 2 * num_sms) {
+    int32_t* order = static_cast<int32_t*>(workspace(stream, static_cast<size_t>(prm.batch) * sizeof(int32_t)));
+    if (order) {
+      lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order);
+      if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+      params.order = order;
+      launches = 2;
+    }
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(G * static_cast<int64_t>(prm.batch)), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -256,8 +305,8 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, prm) != cudaSuccess) return DSA_ERR_CUDA;
-  t_last_launches = 1;
+  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, params) != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = launches;
   return DSA_OK;
 }
 
@@ -309,7 +358,7 @@ extern "C" int dsa_topk_indexer_scores(const void* q, const void* k_cache, const
   p.scores = scores;
   p.score_stride = score_stride;
   rc = launch_indexer<kModeScores>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
-  if (rc == DSA_OK) t_last_launches = 2;
+  if (rc == DSA_OK) t_last_launches += 1;  // the -inf fill
   return rc;
 }
 

@@ -88,6 +88,7 @@ enum MiscWord : int {
 };
 
 struct IndexerParams {
+  const int32_t* order;        // [B] request served by cluster c (longest first), or null
   const int32_t* seq_lens;     // [B]
   const int32_t* block_table;  // [B, max_pages]
   const float* weights;        // [B, 64]
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int lane = threadIdx.x & 31;
   const uint32_t G = ptx::cluster_nctarank();
   const uint32_t rank = ptx::cluster_ctarank();
-  const int b = static_cast<int>(blockIdx.x / G);
+  const int b = p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G);
 
   // ---- request geometry (identical in every thread) ----
   int64_t len = p.seq_lens[b];
@@ -570,6 +571,57 @@ __global__ void __launch_bounds__(kThreads, 2)
       p.cand_pos[o] = live ? static_cast<int32_t>(pos) : -1;
     }
   }
+}
+
+// Longest-first request order for the indexer's clusters (one CTA of 1024
+// threads): counting sort of the rows' tile counts, descending. Rows whose
+// counts fall in the same bucket keep no particular order.
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanBuckets = 4096;
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    lpt_order_kernel(const int32_t* __restrict__ seq_lens, int batch, int max_pages, int32_t* __restrict__ order) {
+  __shared__ uint32_t cnt[kPlanBuckets];
+  __shared__ uint32_t start[kPlanBuckets];
+  __shared__ uint32_t wsum[kPlanThreads / 32];
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int max_tiles = (max_pages + 1) / 2;
+  int shift = 0;
+  while ((max_tiles >> shift) >= kPlanBuckets) ++shift;
+  for (int i = t; i < kPlanBuckets; i += kPlanThreads) cnt[i] = 0u;
+  __syncthreads();
+  auto bucket = [&](int b) {
+    int64_t len = seq_lens[b];
+    len = len < 0 ? 0 : (len > static_cast<int64_t>(max_pages) * kPage ? static_cast<int64_t>(max_pages) * kPage : len);
+    const int tiles = static_cast<int>((len + 2 * kPage - 1) / (2 * kPage));
+    return (kPlanBuckets - 1) - (tiles >> shift);  // descending: longest rows in bucket 0
+  };
+  for (int b = t; b < batch; b += kPlanThreads) atomicAdd(&cnt[bucket(b)], 1u);
+  __syncthreads();
+  // exclusive scan over the 4096 buckets: thread t owns buckets 4t..4t+3
+  uint32_t c[4], tot = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    c[j] = cnt[4 * t + j];
+    tot += c[j];
+  }
+  uint32_t incl = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  uint32_t base = incl - tot;
+  for (int k = 0; k < w; ++k) base += wsum[k];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    start[4 * t + j] = base;
+    base += c[j];
+  }
+  __syncthreads();
+  for (int b = t; b < batch; b += kPlanThreads) order[atomicAdd(&start[bucket(b)], 1u)] = b;
 }
 
 }  // namespace dsa
