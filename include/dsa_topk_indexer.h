@@ -36,6 +36,10 @@ extern "C" {
 #define DSA_ERR_MISALIGNED 2  /* q / k_cache not 16-byte aligned          */
 #define DSA_ERR_CUDA 3        /* a CUDA runtime/driver call failed        */
 #define DSA_ERR_NO_DEVICE 4   /* current device is not sm_100             */
+#define DSA_ERR_TOO_LARGE 5   /* batch above DSA_NOALLOC_MAX_BATCH (no-allocation entry point) */
+
+/* Largest batch dsa_topk_indexer_launch_noalloc accepts. */
+#define DSA_NOALLOC_MAX_BATCH 65536
 
 /* Bits of the per-device status word the kernels raise (sticky until read
  * with clear != 0). */
@@ -89,6 +93,30 @@ DSA_API int dsa_topk_indexer_partial(const void* q, const void* k_cache, const f
 DSA_API int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* cand_pos, int64_t nparts,
                            const int32_t* seq_lens, const int32_t* block_table,
                            int32_t* topk_indices, int64_t batch, int64_t max_pages, void* stream);
+
+/*
+ * Same operation and arguments as dsa_topk_indexer_launch, for callers that
+ * must not allocate device memory: code that runs where cudaMalloc is
+ * forbidden or unsafe (inside a custom allocator, a memory-pool callback, a
+ * tightly budgeted inference server that pre-reserves all of HBM) or that
+ * cannot tolerate the first-call allocation of the launch entry point's
+ * per-stream workspace. It has no counterpart in the reference.
+ *
+ * The scratch it needs (the longest-first row order, 4 bytes per row) lives
+ * in a fixed array inside this library, DSA_NOALLOC_MAX_BATCH rows (256 KiB)
+ * on every GPU that loads the library, held until the process exits. Larger
+ * batches are rejected with DSA_ERR_TOO_LARGE. The first call on a device
+ * looks up that array's device address (with the device current), so make
+ * that first call before any stream capture. All calls on a device share the
+ * array: calls that can overlap on the GPU (different streams, no ordering
+ * between them) race on it and must be serialised by the caller. Nothing in
+ * the array needs clearing between calls; every call rewrites the entries it
+ * reads.
+ */
+DSA_API int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cache, const float* weights,
+                                            const int32_t* seq_lens, const int32_t* block_table,
+                                            int32_t* topk_indices, int64_t batch, int64_t max_pages,
+                                            int64_t num_pages, void* stream);
 
 /* Makes `device` the current CUDA device of the calling host thread for this
  * library (the entry points above run on the current device). Callers that

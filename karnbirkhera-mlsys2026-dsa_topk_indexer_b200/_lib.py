@@ -10,6 +10,8 @@ DSA_ERR_INVALID_ARG = 1
 DSA_ERR_MISALIGNED = 2
 DSA_ERR_CUDA = 3
 DSA_ERR_NO_DEVICE = 4
+DSA_ERR_TOO_LARGE = 5
+DSA_NOALLOC_MAX_BATCH = 65536
 
 DSA_STATUS_WAIT_TIMEOUT = 0x1
 DSA_STATUS_BAD_PAGE = 0x2
@@ -22,6 +24,7 @@ SIGNATURES = [
     ("dsa_topk_indexer_scores", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_partial", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_merge", _I32, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _P]),
+    ("dsa_topk_indexer_launch_noalloc", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_set_device", _I32, [_I32]),
     ("dsa_topk_indexer_status", _I32, [_I32, ctypes.POINTER(ctypes.c_uint32), _I32]),
     ("dsa_topk_indexer_error_string", ctypes.c_char_p, [_I32]),

@@ -399,6 +399,81 @@ extern "C" int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* c
   return DSA_OK;
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation variant of the indexer launch. Its only scratch, the
+// longest-first row order, is this fixed array (4 bytes x
+// DSA_NOALLOC_MAX_BATCH rows) instead of the per-stream workspace. Host code
+// must not pass the array's name to a kernel (in host code it is a host-side
+// stand-in, not a device address): the device address is looked up once per
+// device with cudaGetSymbolAddress, with that device current.
+static __device__ __align__(256) int32_t g_noalloc_order[DSA_NOALLOC_MAX_BATCH];
+
+namespace {
+int32_t* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_order) != cudaSuccess || !ptr) return DSA_ERR_CUDA;
+    g_noalloc_addr[dev] = static_cast<int32_t*>(ptr);
+  }
+  *out = g_noalloc_addr[dev];
+  return DSA_OK;
+}
+}  // namespace
+
+extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cache, const float* weights,
+                                               const int32_t* seq_lens, const int32_t* block_table,
+                                               int32_t* topk_indices, int64_t batch, int64_t max_pages,
+                                               int64_t num_pages, void* stream) {
+  t_last_launches = 0;
+  int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
+  if (rc != DSA_OK || batch == 0) return rc;
+  if (!topk_indices) return DSA_ERR_INVALID_ARG;
+  if (batch > DSA_NOALLOC_MAX_BATCH) return DSA_ERR_TOO_LARGE;
+  int num_sms = 0;
+  rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  int32_t* order = nullptr;
+  rc = noalloc_scratch(&order);
+  if (rc != DSA_OK) return rc;
+  CUtensorMap tk, ts, tq;
+  rc = make_maps(q, k_cache, batch, num_pages, &tk, &ts, &tq);
+  if (rc != DSA_OK) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  p.out = topk_indices;
+  const int G = choose_cluster(batch, max_pages, num_sms);
+  int launches = 1;
+  if (batch > 1 && static_cast<int64_t>(G) * batch > 2 * num_sms) {
+    // The plan kernel writes all `batch` entries the indexer reads.
+    lpt_order_kernel<<<1, kPlanThreads, 0, st>>>(seq_lens, static_cast<int>(batch), static_cast<int>(max_pages),
+                                                 order);
+    if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+    p.order = order;
+    launches = 2;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(G * batch), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(G);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kModeTopK>, tk, ts, tq, p) != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = launches;
+  return DSA_OK;
+}
+
 extern "C" int dsa_topk_indexer_set_device(int device) {
   int cur = -1;
   if (cudaGetDevice(&cur) == cudaSuccess && cur == device) return DSA_OK;
@@ -434,6 +509,8 @@ extern "C" const char* dsa_topk_indexer_error_string(int code) {
       return "CUDA runtime or driver call failed";
     case DSA_ERR_NO_DEVICE:
       return "current device is not an sm_100 (B200) GPU";
+    case DSA_ERR_TOO_LARGE:
+      return "batch exceeds the no-allocation entry point's fixed scratch (DSA_NOALLOC_MAX_BATCH = 65536 rows)";
     default:
       return "unknown error";
   }
