@@ -15,6 +15,7 @@
 
 #include "dsa_topk_indexer.h"
 #include "indexer_kernel.cuh"
+#include "segment_kernels.cuh"
 
 namespace dsa {
 
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
       __syncthreads();
       group_minmax<kMergeThreads, 0>(cand, n, mm, tid);
       thr = group_select<kMergeThreads, 0>(cand, n, kTopK, mm, hist, misc + 4, tid);
-      group_compact<kMergeThreads, 0, kMergeCap / kMergeThreads>(cand, n, thr, misc, tid);
+      group_compact<kMergeThreads, 0, kMergeCap / kMergeThreads>(cand, n, thr, misc, misc + 16, tid);
     }
   }
   __syncthreads();
@@ -150,11 +151,19 @@ int prepare_device(int* num_sms) {
                           reinterpret_cast<const void*>(&indexer_kernel<kModeScores>),
                           reinterpret_cast<const void*>(&indexer_kernel<kModePartial>)};
     for (const void* f : fns) {
-      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess ||
+          cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
         return DSA_ERR_CUDA;
     }
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&merge_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_stream_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kS_SmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_merge_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kM_SmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_merge_kernel),
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return DSA_ERR_CUDA;
     d.ready = true;
   }
@@ -245,10 +254,11 @@ int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_page
 // fewer than about 4 tiles per CTA. Measured on B200: B=64 -> 8 (best of
 // 2/4/8), B=512 -> 2 (best of 1/2/4/8).
 int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
-  // DSA_TOPK_CLUSTER=<1..8> overrides the choice (tuning and tests).
+  // DSA_TOPK_CLUSTER=<1..16> overrides the choice (tuning and tests; sizes
+  // above 8 are a non-portable cluster size B200 supports).
   if (const char* env = std::getenv("DSA_TOPK_CLUSTER")) {
     const int g = std::atoi(env);
-    if (g >= 1 && g <= 8) return g;
+    if (g >= 1 && g <= 16) return g;
   }
   const int64_t tiles = (span_pages + 1) / 2;
   int64_t g = (4 * static_cast<int64_t>(num_sms) + batch - 1) / batch;
@@ -310,6 +320,141 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   return DSA_OK;
 }
 
+int env_int(const char* name, int lo, int hi) {
+  if (const char* e = std::getenv(name)) {
+    const int v = std::atoi(e);
+    if (v >= lo && v <= hi) return v;
+  }
+  return 0;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Segment-scheduled top-K (plan, persistent stream, cluster merge). Returns
+// DSA_ERR_CUDA-free "not taken" (1 in *taken = 0) when the workspace cannot be
+// had (first call on a stream inside capture) or the weights are not 16-byte
+// aligned; the caller then uses the cluster kernel.
+int launch_segmented(const void* q, const void* kcache, const float* w, const IndexerParams& prm, cudaStream_t stream,
+                     bool* taken) {
+  *taken = false;
+  if (!aligned16(w)) return DSA_OK;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  const int64_t B = prm.batch;
+  const int64_t max_tiles = (static_cast<int64_t>(prm.max_pages) + 1) / 2;
+  // Segment length: about 16 segments per resident CTA for the longest
+  // possible rows (8..64 tiles), and at most 16384 workspace slots.
+  int64_t seg = (B * max_tiles + 16 * 2 * num_sms - 1) / (16 * 2 * num_sms);
+  seg = seg < 8 ? 8 : (seg > 64 ? 64 : seg);
+  const int64_t seg_floor = (B * max_tiles + 16383) / 16384;
+  if (seg < seg_floor) seg = seg_floor;
+  if (int v = env_int("DSA_TOPK_SEG", 2, 1 << 20)) seg = v;
+  seg += seg & 1;
+  const int64_t s_max = (max_tiles + seg - 1) / seg;
+  const int64_t slots = B * (s_max > 0 ? s_max : 1);
+  // Workspace carve-up.
+  size_t off = 0;
+  const size_t o_ctrl = off;
+  off = align256(off + 256);
+  const size_t o_order = off;
+  off = align256(off + 4 * B);
+  const size_t o_first = off;
+  off = align256(off + 4 * B);
+  const size_t o_cnt = off;
+  off = align256(off + 4 * B);
+  const size_t o_segs = off;
+  off = align256(off + 16 * slots);
+  const size_t o_n = off;
+  off = align256(off + 4 * slots);
+  const size_t o_cand = off;
+  off = align256(off + static_cast<size_t>(8) * kCap * slots);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(stream, off));
+  if (!ws) return DSA_OK;
+  CUtensorMap tk, ts, tq, tw;
+  rc = make_maps(q, kcache, B, prm.num_pages, &tk, &ts, &tq);
+  if (rc != DSA_OK) return rc;
+  {  // weights: {64 fp32, B}, box = one row
+    EncodeTiledFn enc = encode_fn();
+    std::memset(&tw, 0, sizeof(tw));
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeads), static_cast<cuuint64_t>(B)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeads * 4)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kHeads), 1};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return DSA_ERR_CUDA;
+  }
+  SegPlan pl;
+  pl.ctrl = reinterpret_cast<uint32_t*>(ws + o_ctrl);
+  pl.order = reinterpret_cast<int32_t*>(ws + o_order);
+  pl.seg_first = reinterpret_cast<int32_t*>(ws + o_first);
+  pl.seg_cnt = reinterpret_cast<int32_t*>(ws + o_cnt);
+  pl.segs = reinterpret_cast<int4*>(ws + o_segs);
+  segment_plan_kernel<<<1, kSegPlanThreads, 0, stream>>>(prm.seq_lens, static_cast<int>(B), prm.max_pages,
+                                                         static_cast<int>(seg), pl);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  StreamParams sp;
+  sp.seq_lens = prm.seq_lens;
+  sp.block_table = prm.block_table;
+  sp.segs = pl.segs;
+  sp.ctrl = pl.ctrl;
+  sp.ws_cand = reinterpret_cast<uint64_t*>(ws + o_cand);
+  sp.ws_n = reinterpret_cast<uint32_t*>(ws + o_n);
+  sp.num_pages = prm.num_pages;
+  sp.max_pages = prm.max_pages;
+  sp.batch = prm.batch;
+  // The stream and merge kernels are programmatic dependents of the kernel
+  // before them: they launch and set up while it drains, and wait for its
+  // results with griddepcontrol.wait (DSA_TOPK_PDL=0 turns this off).
+  const char* pdl_env = std::getenv("DSA_TOPK_PDL");
+  const bool pdl = !(pdl_env && pdl_env[0] == '0');
+  {
+    cudaLaunchConfig_t scfg{};
+    scfg.gridDim = dim3(static_cast<unsigned>(2 * num_sms), 1, 1);
+    scfg.blockDim = dim3(kThreads, 1, 1);
+    scfg.dynamicSmemBytes = kS_SmemBytes;
+    scfg.stream = stream;
+    cudaLaunchAttribute sattr[1];
+    sattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    sattr[0].val.programmaticStreamSerializationAllowed = 1;
+    scfg.attrs = sattr;
+    scfg.numAttrs = pdl ? 1 : 0;
+    if (cudaLaunchKernelEx(&scfg, segment_stream_kernel, tk, ts, tq, tw, sp) != cudaSuccess) return DSA_ERR_CUDA;
+  }
+  // Merge: clusters of Gm CTAs per row, enough to cover the GPU about twice.
+  int64_t gm = (2 * num_sms + B - 1) / B;
+  if (gm > s_max) gm = s_max;
+  if (gm > 8) gm = 8;
+  if (gm < 1) gm = 1;
+  if (int v = env_int("DSA_TOPK_MERGE_CLUSTER", 1, 16)) gm = v;
+  MergeParams mp;
+  mp.order = pl.order;
+  mp.seg_first = pl.seg_first;
+  mp.seg_cnt = pl.seg_cnt;
+  mp.ws_cand = sp.ws_cand;
+  mp.ws_n = sp.ws_n;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(gm * B), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kM_SmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(gm);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  if (cudaLaunchKernelEx(&cfg, segment_merge_kernel, mp, prm) != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 3;
+  *taken = true;
+  return DSA_OK;
+}
+
 IndexerParams base_params(const float* w, const int32_t* sl, const int32_t* bt, int64_t batch, int64_t max_pages,
                           int64_t num_pages) {
   IndexerParams p{};
@@ -336,6 +481,13 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
   IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
+  // DSA_TOPK_PATH=cluster forces the one-launch cluster kernel (tests).
+  const char* path = std::getenv("DSA_TOPK_PATH");
+  if (!(path && std::strcmp(path, "cluster") == 0)) {
+    bool taken = false;
+    rc = launch_segmented(q, k_cache, weights, p, static_cast<cudaStream_t>(stream), &taken);
+    if (rc != DSA_OK || taken) return rc;
+  }
   return launch_indexer<kModeTopK>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
 }
 

@@ -81,7 +81,6 @@ enum MiscWord : int {
   kMiscPub = 8,    // 2 words read by other CTAs of the cluster
   kMiscTotal = 10,
   kMiscOffset = 11,
-  kMiscWrite = 12,
   kMiscMM = 16,     // 2 x u64: min / max of the local candidates
   kMiscPubMM = 20,  // 2 x u64 read by other CTAs of the cluster
   kMiscWsum = 24,   // 8 words: scan scratch of the final ordering
@@ -139,6 +138,155 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
   }
 }
 
+// Cluster-wide exact selection of the best 2048 of all candidates held by the
+// G CTAs of this cluster (n in this CTA's cand buffer), survivors gathered in
+// CTA 0's shared memory, ordered and emitted for row b. Called by all
+// kThreads threads of every CTA of the cluster, with the K ring free. Shared
+// by the streaming cluster kernel and the segment merge kernel, which use the
+// same shared-memory map.
+// Shared-memory offsets cluster_select_emit works with. `Final` receives the
+// survivors of every CTA (written remotely) and must not overlap `Cand`;
+// the ordering scratch (`RankTmp`, `RankCnt`) is only touched after the last
+// cluster barrier, when `Cand` is dead.
+struct StreamSelectLayout {
+  static constexpr int kCand = kOffCand, kHist = kOffHist, kTot = kOffTot, kMisc = kOffMisc;
+  static constexpr int kFinal = kOffFinal, kRankTmp = kOffRankTmp, kRankCnt = kOffRankCnt;
+};
+
+template <int kMode, class L>
+__device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base_addr, uint32_t n, uint32_t G,
+                                                    uint32_t rank, int b, const int32_t* bt_row,
+                                                    const IndexerParams& p) {
+  uint64_t* cand = reinterpret_cast<uint64_t*>(smem + L::kCand);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L::kHist);
+  uint32_t* tot = reinterpret_cast<uint32_t*>(smem + L::kTot);
+  uint32_t* misc_nv = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  unsigned long long* mm = reinterpret_cast<unsigned long long*>(smem + L::kMisc + 4 * kMiscMM);
+  unsigned long long* pub_mm = reinterpret_cast<unsigned long long*>(smem + L::kMisc + 4 * kMiscPubMM);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // ---- cluster-wide exact selection of the best 2048 keys ----
+  const int tid = threadIdx.x;
+  const uint32_t pub_addr = base_addr + L::kMisc + 4 * kMiscPub;
+  const uint32_t pub_mm_addr = base_addr + L::kMisc + 4 * kMiscPubMM;
+  if (tid == 0) {
+    mm[0] = ~0ull;
+    mm[1] = 0ull;
+  }
+  __syncthreads();
+  group_minmax<kThreads, 0>(cand, n, mm, tid);
+  if (tid == 0) {
+    misc_nv[kMiscPub] = n;
+    pub_mm[0] = mm[0];
+    pub_mm[1] = mm[1];
+  }
+  ptx::cluster_sync();
+  if (warp == 0) {
+    // Cluster totals: candidate count, smallest and largest key.
+    uint32_t v = 0;
+    unsigned long long lo = ~0ull, hi = 0ull;
+    if (static_cast<uint32_t>(lane) < G) {
+      v = ptx::ld_dsmem_u32(ptx::mapa(pub_addr, lane));
+      const uint32_t a = ptx::mapa(pub_mm_addr, lane);
+      lo = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 4)) << 32) | ptx::ld_dsmem_u32(a);
+      hi = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 12)) << 32) | ptx::ld_dsmem_u32(a + 8);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+      const unsigned long long x = __shfl_xor_sync(0xFFFFFFFFu, lo, off);
+      const unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, hi, off);
+      lo = x < lo ? x : lo;
+      hi = y > hi ? y : hi;
+    }
+    if (lane == 0) {
+      misc_nv[kMiscTotal] = v;
+      mm[0] = lo;
+      mm[1] = hi;
+    }
+  }
+  __syncthreads();
+  const uint32_t total = misc_nv[kMiscTotal];
+  uint64_t T = 0;
+  if (total > static_cast<uint32_t>(kTopK)) {
+    RadixState st = radix_start(mm[0], mm[1], kTopK);
+    int pass = 0;
+#pragma unroll 1
+    while (true) {
+      uint32_t* hb = hist + (pass & 1) * 256;
+      if (tid < 256) hb[tid] = 0u;
+      __syncthreads();
+      radix_hist<kThreads>(cand, n, st, hb, tid);
+      ptx::cluster_sync();  // every CTA's histogram of this pass is complete
+      if (tid < 256) {
+        const uint32_t hb_addr = ptx::smem_addr(hb + tid);
+        uint32_t sum = 0;
+        for (uint32_t r = 0; r < G; ++r) sum += ptx::ld_dsmem_u32(ptx::mapa(hb_addr, r));
+        tot[tid] = sum;
+      }
+      __syncthreads();
+      if (warp == 0) find_digit_warp(tot, st.krem, misc_nv + kMiscSel);
+      __syncthreads();
+      if (radix_advance(st, misc_nv + kMiscSel)) break;
+      ++pass;
+    }
+    T = st.prefix;
+  }
+  // Count this CTA's survivors per warp (each warp owns a contiguous range of
+  // the buffer), publish the CTA total, and get this CTA's output offset.
+  const uint32_t nsel = total < static_cast<uint32_t>(kTopK) ? total : static_cast<uint32_t>(kTopK);
+  uint32_t wlo, whi;
+  warp_range(n, warp, kThreads / 32, &wlo, &whi);
+  const uint32_t wc = warp_count_ge(cand, wlo, whi, T);
+  if (lane == 0) tot[warp] = wc;  // the digit totals are no longer needed
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t c = 0;
+    for (int k = 0; k < kThreads / 32; ++k) c += tot[k];
+    misc_nv[kMiscPub + 1] = c;
+  }
+  ptx::cluster_sync();
+  if (warp == 0) {
+    uint32_t v = (static_cast<uint32_t>(lane) < rank) ? ptx::ld_dsmem_u32(ptx::mapa(pub_addr + 4, lane)) : 0u;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
+    if (lane == 0) misc_nv[kMiscOffset] = v;
+  }
+  __syncthreads();
+  {
+    uint32_t off = misc_nv[kMiscOffset];
+    for (int k = 0; k < warp; ++k) off += tot[k];
+    warp_write_ge(cand, wlo, whi, T, ptx::mapa(base_addr + L::kFinal, 0) + 8u * off);
+  }
+  ptx::cluster_sync();
+  if (rank != 0 || tid >= 256) return;
+
+  // ---- CTA 0, threads 0..255: order the survivors and emit ----
+  uint64_t* fin = reinterpret_cast<uint64_t*>(smem + L::kFinal);
+  RankScratch sc;
+  sc.tmp = reinterpret_cast<uint64_t*>(smem + L::kRankTmp);
+  sc.cnt = reinterpret_cast<uint32_t*>(smem + L::kRankCnt);
+  sc.start = sc.cnt + 2048;
+  sc.fill = sc.start + 2048;
+  sc.wsum = misc_nv + kMiscWsum;
+  sc.mm = mm;
+  block_rank_order<kBarLow>(fin, nsel, sc);
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
+    const bool live = i < nsel;
+    const uint64_t key = live ? fin[i] : 0ull;
+    const uint32_t pos = key_pos(key);
+    const int64_t o = static_cast<int64_t>(b) * kTopK + i;
+    if (kMode == kModeTopK) {
+      p.out[o] = live ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
+    } else {
+      p.cand_scores[o] = live ? ordered_to_float(static_cast<uint32_t>(key >> 32)) : -__int_as_float(0x7f800000);
+      p.cand_pos[o] = live ? static_cast<int32_t>(pos) : -1;
+    }
+  }
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 2)
     indexer_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
@@ -150,13 +298,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem + kOffCand);
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kOffHist);
-  uint32_t* tot = reinterpret_cast<uint32_t*>(smem + kOffTot);
   float* s_w = reinterpret_cast<float*>(smem + kOffW);
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(smem + kOffMisc);
   uint32_t* misc_nv = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile uint32_t* abort_flag = misc + kMiscAbort;
   unsigned long long* mm = reinterpret_cast<unsigned long long*>(smem + kOffMisc + 4 * kMiscMM);
-  unsigned long long* pub_mm = reinterpret_cast<unsigned long long*>(smem + kOffMisc + 4 * kMiscPubMM);
 
   const uint32_t bar_full = base_addr + kOffBar;                // [kStages]
   const uint32_t bar_empty = bar_full + 8 * kStages;            // [kStages]
@@ -208,8 +354,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     ptx::fence_mbar_init();
     misc_nv[kMiscCount] = 0u;
     misc_nv[kMiscAbort] = 0u;
-    misc_nv[kMiscPub + 1] = 0u;
-    misc_nv[kMiscWrite] = 0u;
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_s);
     ptx::prefetch_tmap(&tm_q);
@@ -405,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               uint64_t T = group_cut<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, &kept);
               if (kept > static_cast<uint32_t>(kCap - 4 * kTileKeys))
                 T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
-              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, et);
+              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, misc_nv + kMiscWsum, et);
               thr = T;
               n = misc[kMiscCount];
             }
@@ -441,136 +585,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (kMode == kModeScores) return;
 
-  // ---- cluster-wide exact selection of the best 2048 keys ----
-  const int tid = threadIdx.x;
-  const uint32_t n = misc_nv[kMiscCount];
-  const uint32_t pub_addr = base_addr + kOffMisc + 4 * kMiscPub;
-  const uint32_t pub_mm_addr = base_addr + kOffMisc + 4 * kMiscPubMM;
-  if (tid == 0) {
-    mm[0] = ~0ull;
-    mm[1] = 0ull;
-  }
-  __syncthreads();
-  group_minmax<kThreads, 0>(cand, n, mm, tid);
-  if (tid == 0) {
-    misc_nv[kMiscPub] = n;
-    pub_mm[0] = mm[0];
-    pub_mm[1] = mm[1];
-  }
-  ptx::cluster_sync();
-  if (warp == 0) {
-    // Cluster totals: candidate count, smallest and largest key.
-    uint32_t v = 0;
-    unsigned long long lo = ~0ull, hi = 0ull;
-    if (static_cast<uint32_t>(lane) < G) {
-      v = ptx::ld_dsmem_u32(ptx::mapa(pub_addr, lane));
-      const uint32_t a = ptx::mapa(pub_mm_addr, lane);
-      lo = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 4)) << 32) | ptx::ld_dsmem_u32(a);
-      hi = (static_cast<unsigned long long>(ptx::ld_dsmem_u32(a + 12)) << 32) | ptx::ld_dsmem_u32(a + 8);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-      const unsigned long long x = __shfl_xor_sync(0xFFFFFFFFu, lo, off);
-      const unsigned long long y = __shfl_xor_sync(0xFFFFFFFFu, hi, off);
-      lo = x < lo ? x : lo;
-      hi = y > hi ? y : hi;
-    }
-    if (lane == 0) {
-      misc_nv[kMiscTotal] = v;
-      mm[0] = lo;
-      mm[1] = hi;
-    }
-  }
-  __syncthreads();
-  const uint32_t total = misc_nv[kMiscTotal];
-  uint64_t T = 0;
-  if (total > static_cast<uint32_t>(kTopK)) {
-    RadixState st = radix_start(mm[0], mm[1], kTopK);
-    int pass = 0;
-#pragma unroll 1
-    while (true) {
-      uint32_t* hb = hist + (pass & 1) * 256;
-      if (tid < 256) hb[tid] = 0u;
-      __syncthreads();
-      radix_hist<kThreads>(cand, n, st, hb, tid);
-      ptx::cluster_sync();  // every CTA's histogram of this pass is complete
-      if (tid < 256) {
-        const uint32_t hb_addr = ptx::smem_addr(hb + tid);
-        uint32_t sum = 0;
-        for (uint32_t r = 0; r < G; ++r) sum += ptx::ld_dsmem_u32(ptx::mapa(hb_addr, r));
-        tot[tid] = sum;
-      }
-      __syncthreads();
-      if (warp == 0) find_digit_warp(tot, st.krem, misc_nv + kMiscSel);
-      __syncthreads();
-      if (radix_advance(st, misc_nv + kMiscSel)) break;
-      ++pass;
-    }
-    T = st.prefix;
-  }
-  // Count this CTA's survivors, publish, and get this CTA's output offset.
-  {
-    uint32_t c = 0;
-    for (uint32_t i = tid; i < n; i += kThreads) c += (cand[i] >= T) ? 1u : 0u;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, off);
-    if (lane == 0 && c) atomicAdd(misc_nv + kMiscPub + 1, c);
-  }
-  ptx::cluster_sync();
-  if (warp == 0) {
-    uint32_t v = (static_cast<uint32_t>(lane) < rank) ? ptx::ld_dsmem_u32(ptx::mapa(pub_addr + 4, lane)) : 0u;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
-    if (lane == 0) misc_nv[kMiscOffset] = v;
-  }
-  __syncthreads();
-  const uint32_t nsel = total < static_cast<uint32_t>(kTopK) ? total : static_cast<uint32_t>(kTopK);
-  {
-    const uint32_t my_off = misc_nv[kMiscOffset];
-    const uint32_t fin_remote = ptx::mapa(base_addr + kOffFinal, 0);
-#pragma unroll 1
-    for (uint32_t i0 = 0; i0 < n; i0 += kThreads) {
-      const uint32_t i = i0 + tid;
-      const uint64_t key = (i < n) ? cand[i] : 0ull;
-      const bool keep = (i < n) && key >= T;
-      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
-      if (m) {
-        const int leader = __ffs(m) - 1;
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(misc_nv + kMiscWrite, static_cast<uint32_t>(__popc(m)));
-        base = __shfl_sync(0xFFFFFFFFu, base, leader);
-        if (keep) ptx::st_dsmem_u64(fin_remote + 8u * (my_off + base + __popc(m & lanemask_lt())), key);
-      }
-    }
-  }
-  ptx::cluster_sync();
-  if (rank != 0 || tid >= 256) return;
-
-  // ---- CTA 0, threads 0..255: order the survivors and emit ----
-  uint64_t* fin = reinterpret_cast<uint64_t*>(smem + kOffFinal);
-  RankScratch sc;
-  sc.tmp = reinterpret_cast<uint64_t*>(smem + kOffRankTmp);
-  sc.cnt = reinterpret_cast<uint32_t*>(smem + kOffRankCnt);
-  sc.start = sc.cnt + 2048;
-  sc.fill = sc.start + 2048;
-  sc.wsum = misc_nv + kMiscWsum;
-  sc.mm = mm;
-  block_rank_order<kBarLow>(fin, nsel, sc);
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
-    const bool live = i < nsel;
-    const uint64_t key = live ? fin[i] : 0ull;
-    const uint32_t pos = key_pos(key);
-    const int64_t o = static_cast<int64_t>(b) * kTopK + i;
-    if (kMode == kModeTopK) {
-      p.out[o] = live ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
-    } else {
-      p.cand_scores[o] = live ? ordered_to_float(static_cast<uint32_t>(key >> 32)) : -__int_as_float(0x7f800000);
-      p.cand_pos[o] = live ? static_cast<int32_t>(pos) : -1;
-    }
-  }
+  cluster_select_emit<kMode, StreamSelectLayout>(smem, base_addr, misc_nv[kMiscCount], G, rank, b, bt_row, p);
 }
 
 // Longest-first request order for the indexer's clusters (one CTA of 1024

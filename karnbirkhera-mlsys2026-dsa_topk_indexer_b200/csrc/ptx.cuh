@@ -284,5 +284,19 @@ __device__ __forceinline__ void named_bar(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Asynchronous 8-byte global -> shared copy (both addresses 8-byte aligned);
+// completes at cp_async_wait_all of the issuing thread.
+__device__ __forceinline__ void cp_async8(uint32_t dst_smem, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Programmatic dependent launch: grid_dep_wait blocks until the grid this one
+// depends on has completed and its memory is visible (returns at once when
+// the kernel was launched without that dependency); grid_dep_launch lets the
+// dependent grid start launching before this one ends.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace ptx
 }  // namespace dsa

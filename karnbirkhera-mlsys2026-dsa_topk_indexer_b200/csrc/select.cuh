@@ -137,7 +137,17 @@ __device__ __forceinline__ void radix_hist(const uint64_t* cand, uint32_t n, con
   const int shift = 64 - st.top - width;
   const uint64_t hm = high_mask(st.top);
   const uint32_t dmask = (1u << width) - 1u;
-  for (uint32_t i = gt; i < n; i += NT) {
+  uint32_t i = gt;
+  // Four keys per step, loaded before any of their (non-returning) atomics.
+  for (; i + 3 * NT < n; i += 4 * NT) {
+    uint64_t k[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) k[u] = cand[i + u * NT];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if ((k[u] & hm) == st.prefix) atomicAdd(&hist[static_cast<uint32_t>(k[u] >> shift) & dmask], 1u);
+  }
+  for (; i < n; i += NT) {
     const uint64_t key = cand[i];
     if ((key & hm) == st.prefix) atomicAdd(&hist[static_cast<uint32_t>(key >> shift) & dmask], 1u);
   }
@@ -193,33 +203,93 @@ __device__ uint64_t group_cut(const uint64_t* cand, uint32_t n, uint32_t k, cons
   return st.prefix | (static_cast<uint64_t>(sel[0]) << (64 - st.top - width));
 }
 
+// Exclusive offset of this warp's count among the NT/32 warps of a group,
+// and the group total. wsum: NT/32 words; one group barrier inside, and the
+// caller must pass another barrier before wsum is written again.
+template <int NT, int BAR>
+__device__ __forceinline__ uint32_t group_warp_offset(uint32_t wcount, uint32_t* wsum, uint32_t* total, int gt) {
+  const int gw = gt >> 5;
+  if ((gt & 31) == 0) wsum[gw] = wcount;
+  group_sync<NT, BAR>();
+  uint32_t base = 0, tot = 0;
+#pragma unroll
+  for (int k = 0; k < NT / 32; ++k) {
+    const uint32_t x = wsum[k];
+    base += (k < gw) ? x : 0u;
+    tot += x;
+  }
+  *total = tot;
+  return base;
+}
+
 // Keeps the keys >= T of cand[0..n) and packs them to the front; `counter`
-// ends holding the number kept. MAXPER >= ceil(n / NT).
+// ends holding the number kept. MAXPER >= ceil(n / NT). The keys are held in
+// registers, so the packing is in place; output slots come from per-warp
+// ballot counts and one offset scan (no returning atomics in the loop).
 template <int NT, int BAR, int MAXPER>
-__device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* counter, int gt) {
+__device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* counter, uint32_t* wsum, int gt) {
+  const int lane = threadIdx.x & 31;
   uint64_t v[MAXPER];
+  uint32_t m[MAXPER];
+  uint32_t cnt = 0;
 #pragma unroll
   for (int j = 0; j < MAXPER; ++j) {
     const uint32_t i = gt + j * NT;
     v[j] = (i < n) ? cand[i] : 0ull;
   }
-  if (gt == 0) *counter = 0u;
-  group_sync<NT, BAR>();
-  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int j = 0; j < MAXPER; ++j) {
     const uint32_t i = gt + j * NT;
-    const bool keep = (i < n) && (v[j] >= T);
-    const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
-    if (m) {
-      const int leader = __ffs(m) - 1;
-      uint32_t base = 0;
-      if (lane == leader) base = atomicAdd(counter, static_cast<uint32_t>(__popc(m)));
-      base = __shfl_sync(0xFFFFFFFFu, base, leader);
-      if (keep) cand[base + __popc(m & lanemask_lt())] = v[j];
-    }
+    m[j] = __ballot_sync(0xFFFFFFFFu, (i < n) && (v[j] >= T));
+    cnt += static_cast<uint32_t>(__popc(m[j]));
   }
+  uint32_t total = 0;
+  uint32_t base = group_warp_offset<NT, BAR>(cnt, wsum, &total, gt);  // every load is done past this barrier
+#pragma unroll
+  for (int j = 0; j < MAXPER; ++j) {
+    if ((m[j] >> lane) & 1u) cand[base + __popc(m[j] & lanemask_lt())] = v[j];
+    base += static_cast<uint32_t>(__popc(m[j]));
+  }
+  if (gt == 0) *counter = total;
   group_sync<NT, BAR>();
+}
+
+// Survivor count (keys >= T) of src[lo, hi), by one warp over consecutive
+// 32-key rows (loads are independent, so the loop pipelines).
+__device__ __forceinline__ uint32_t warp_count_ge(const uint64_t* src, uint32_t lo, uint32_t hi, uint64_t T) {
+  const int lane = threadIdx.x & 31;
+  uint32_t c = 0;
+#pragma unroll 4
+  for (uint32_t i0 = lo; i0 < hi; i0 += 32) {
+    const uint32_t i = i0 + lane;
+    const uint64_t k = i < hi ? src[i] : 0ull;
+    c += static_cast<uint32_t>(__popc(__ballot_sync(0xFFFFFFFFu, i < hi && k >= T)));
+  }
+  return c;
+}
+
+// Writes the keys >= T of src[lo, hi) (same warp and rows as warp_count_ge)
+// to consecutive 8-byte slots from shared::cluster address dst (this CTA's
+// or another CTA's shared memory).
+__device__ __forceinline__ void warp_write_ge(const uint64_t* src, uint32_t lo, uint32_t hi, uint64_t T,
+                                              uint32_t dst) {
+  const int lane = threadIdx.x & 31;
+  for (uint32_t i0 = lo; i0 < hi; i0 += 32) {
+    const uint32_t i = i0 + lane;
+    const uint64_t k = i < hi ? src[i] : 0ull;
+    const bool keep = i < hi && k >= T;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+    if (keep) ptx::st_dsmem_u64(dst + 8u * static_cast<uint32_t>(__popc(m & lanemask_lt())), k);
+    dst += 8u * static_cast<uint32_t>(__popc(m));
+  }
+}
+
+// The warp-contiguous row range of warp gw (of NW) over n keys.
+__device__ __forceinline__ void warp_range(uint32_t n, int gw, int NW, uint32_t* lo, uint32_t* hi) {
+  const uint32_t chunk = ((n + NW * 32 - 1) / (NW * 32)) * 32;
+  const uint32_t a = static_cast<uint32_t>(gw) * chunk;
+  *lo = a < n ? a : n;
+  *hi = a + chunk < n ? a + chunk : n;
 }
 
 // Shared-memory scratch of block_rank_order (all arrays 2048 long).
@@ -236,11 +306,18 @@ struct RankScratch {
 // 256 threads (t = 0..255) synchronised by barrier BAR. Instead of a sorting
 // network (which on 256 threads is bound by shared-memory traffic or shuffle
 // latency at tens of thousands of cycles for 2048 64-bit keys), keys are
-// counted into 2048 buckets on the 11 bits just below their common prefix,
-// scattered bucket by bucket, and each key's final rank is the number of
-// keys in higher buckets plus the number of larger keys in its own bucket.
-// Exact for any input; a bucket holds a handful of keys for continuous
-// scores and the cost only grows when very many keys share their top bits.
+// counted into 2048 buckets, scattered bucket by bucket, and each key's final
+// rank is the number of keys in higher buckets plus the number of larger keys
+// in its own bucket. Exact for any input as long as the bucket of a key is a
+// non-decreasing function of the key.
+//
+// Buckets split the score range [min, max] of the keys linearly, so the cost
+// stays a handful of comparisons per key however the range sits relative to
+// powers of two (a window of key bits would put the whole set into one or
+// two buckets whenever the range crosses one, since the first differing bits
+// are then exponent bits). When the score range is empty or not finite the
+// 11 key bits below the keys' common prefix are used instead (equal scores
+// then spread by position).
 template <int BAR>
 __device__ __noinline__ void block_rank_order(uint64_t* keys, uint32_t n, const RankScratch sc) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -254,10 +331,23 @@ __device__ __noinline__ void block_rank_order(uint64_t* keys, uint32_t n, const 
   }
   group_sync<256, BAR>();
   group_minmax<256, BAR>(keys, n, sc.mm, t);
-  const uint64_t x = sc.mm[0] ^ sc.mm[1];
+  const uint64_t kmin = sc.mm[0], kmax = sc.mm[1];
+  const float smin = ordered_to_float(static_cast<uint32_t>(kmin >> 32));
+  const float smax = ordered_to_float(static_cast<uint32_t>(kmax >> 32));
+  const float range = smax - smin;
+  const float scale = 2048.f / range;
+  const bool lin = isfinite(smin) && isfinite(smax) && range > 0.f && isfinite(range) && isfinite(scale);
+  const uint64_t x = kmin ^ kmax;
   const int top = x ? __clzll(static_cast<long long>(x)) : 64;
   const int shift = (64 - top - 11) > 0 ? (64 - top - 11) : 0;
-  for (uint32_t i = t; i < n; i += 256) atomicAdd(&sc.cnt[static_cast<uint32_t>(keys[i] >> shift) & 2047u], 1u);
+  auto bucket = [&](uint64_t k) -> uint32_t {
+    if (lin) {
+      const float f = (ordered_to_float(static_cast<uint32_t>(k >> 32)) - smin) * scale;
+      return f >= 2047.f ? 2047u : static_cast<uint32_t>(f);
+    }
+    return static_cast<uint32_t>(k >> shift) & 2047u;
+  };
+  for (uint32_t i = t; i < n; i += 256) atomicAdd(&sc.cnt[bucket(keys[i])], 1u);
   group_sync<256, BAR>();
   // Exclusive scan in descending bucket order; thread t owns buckets
   // 2047-8t down to 2040-8t.
@@ -285,13 +375,13 @@ __device__ __noinline__ void block_rank_order(uint64_t* keys, uint32_t n, const 
   group_sync<256, BAR>();
   for (uint32_t i = t; i < n; i += 256) {
     const uint64_t k = keys[i];
-    const uint32_t d = static_cast<uint32_t>(k >> shift) & 2047u;
+    const uint32_t d = bucket(k);
     sc.tmp[sc.start[d] + atomicAdd(&sc.fill[d], 1u)] = k;
   }
   group_sync<256, BAR>();
   for (uint32_t i = t; i < n; i += 256) {
     const uint64_t k = sc.tmp[i];
-    const uint32_t d = static_cast<uint32_t>(k >> shift) & 2047u;
+    const uint32_t d = bucket(k);
     const uint32_t b0 = sc.start[d], b1 = b0 + sc.cnt[d];
     uint32_t r0 = 0, r1 = 0;
     uint32_t q = b0;

@@ -244,3 +244,36 @@ def test_forced_cluster_sizes_l2_resident(pkg, g, monkeypatch):
     monkeypatch.setenv("DSA_TOPK_CLUSTER", str(g))
     w = workloads().make_shared("l2res", 192, 9000, 160, 21)
     assert_parity(pkg, _rows(w, list(range(0, 192, 3))))
+
+
+@pytest.mark.parametrize("seg,gm", [(2, 1), (4, 3), (8, 8), (16, 2), (64, 1)])
+def test_segmented_path_segment_and_merge_sizes(pkg, seg, gm, monkeypatch):
+    """The segment-scheduled path for several segment lengths and merge
+    cluster sizes: rows shorter than, equal to and much longer than one
+    segment, an empty row, odd tile counts."""
+    monkeypatch.setenv("DSA_TOPK_SEG", str(seg))
+    monkeypatch.setenv("DSA_TOPK_MERGE_CLUSTER", str(gm))
+    w = workloads().custom([0, 64, 130, 2049, 4097, 12345, 33000, 300], seed=23)
+    assert_parity(pkg, w)
+
+
+@pytest.mark.parametrize("gm", [1, 3])
+def test_segmented_merge_many_short_lists(pkg, gm, monkeypatch):
+    """Segments of two tiles on rows of up to 131072 keys: a merge CTA gets
+    more lists than it has threads and more keys than its buffer holds, so
+    it takes several rounds of list copies with exact cuts in between."""
+    monkeypatch.setenv("DSA_TOPK_SEG", "2")
+    monkeypatch.setenv("DSA_TOPK_MERGE_CLUSTER", str(gm))
+    w = workloads().custom([131072, 65543, 1, 20000], seed=29)
+    assert_parity(pkg, w)
+
+
+@pytest.mark.parametrize("cfg", [1, 3])
+def test_cluster_kernel_path(pkg, cfg, monkeypatch):
+    """The one-launch cluster kernel (used when no workspace can be had, and
+    by the no-allocation entry point) stays parity-green."""
+    monkeypatch.setenv("DSA_TOPK_PATH", "cluster")
+    w = workloads().config(cfg)
+    if cfg == 3:
+        w = _rows(w, list(range(0, 8192, 37)))
+    assert_parity(pkg, w)
