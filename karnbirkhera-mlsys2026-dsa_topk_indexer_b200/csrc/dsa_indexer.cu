@@ -81,22 +81,20 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
   }
   __syncthreads();
   const uint32_t nsel = misc[0] < static_cast<uint32_t>(kTopK) ? misc[0] : static_cast<uint32_t>(kTopK);
+  if (tid == 0) {
+    mm[0] = ~0ull;
+    mm[1] = 0ull;
+  }
+  __syncthreads();
+  group_minmax<kMergeThreads, 0>(cand, nsel, mm, tid);
   RankScratch sc;
   sc.tmp = cand + kTopK;
   sc.cnt = rank_cnt;
   sc.start = rank_cnt + 2048;
   sc.fill = rank_cnt + 4096;
   sc.wsum = misc + 16;
-  sc.mm = mm;
-  block_rank_order<0>(cand, nsel, sc);
-  const int32_t* bt_row = block_table + static_cast<int64_t>(b) * max_pages;
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
-    const uint32_t pos = i < nsel ? key_pos(cand[i]) : 0u;
-    out[static_cast<int64_t>(b) * kTopK + i] =
-        (i < nsel) ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
-  }
+  EmitSlots e{out + static_cast<int64_t>(b) * kTopK, block_table + static_cast<int64_t>(b) * max_pages};
+  block_rank_emit<0>(cand, nsel, mm[0], mm[1], sc, e);
 }
 
 // Fills a float buffer (used for the -inf background of the score rows).
@@ -132,12 +130,13 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   bool ready = false;
   int num_sms = 148;
+  int64_t l2_bytes = 0;
 };
 DeviceInfo g_devices[kMaxDevices];
 std::mutex g_dev_mutex;
 
 // Per-device one-time set-up: architecture check and kernel attributes.
-int prepare_device(int* num_sms) {
+int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DSA_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_dev_mutex);
@@ -147,6 +146,7 @@ int prepare_device(int* num_sms) {
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return DSA_ERR_CUDA;
     if (prop.major != 10 || prop.minor != 0) return DSA_ERR_NO_DEVICE;
     d.num_sms = prop.multiProcessorCount;
+    d.l2_bytes = prop.l2CacheSize;
     const void* fns[3] = {reinterpret_cast<const void*>(&indexer_kernel<kModeTopK>),
                           reinterpret_cast<const void*>(&indexer_kernel<kModeScores>),
                           reinterpret_cast<const void*>(&indexer_kernel<kModePartial>)};
@@ -168,6 +168,7 @@ int prepare_device(int* num_sms) {
     d.ready = true;
   }
   *num_sms = d.num_sms;
+  if (l2_bytes) *l2_bytes = d.l2_bytes;
   return DSA_OK;
 }
 
@@ -181,6 +182,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 struct Workspace {
   void* ptr = nullptr;
   size_t bytes = 0;
+  // Second stream for a concurrent launch, with the events that fork it
+  // from and join it back to the caller's stream (created outside capture).
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 std::map<std::pair<int, cudaStream_t>, Workspace> g_workspaces;
 std::vector<void*> g_retired;
@@ -204,6 +209,35 @@ void* workspace(cudaStream_t stream, size_t bytes) {
   ws.ptr = fresh;
   ws.bytes = want;
   return ws.ptr;
+}
+
+// The side stream and fork/join events of (current device, stream); false if
+// they would have to be created while the stream is being captured.
+bool side_stream(cudaStream_t stream, cudaStream_t* side, cudaEvent_t* fork, cudaEvent_t* join) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  Workspace& ws = g_workspaces[{dev, stream}];
+  if (!ws.side) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return false;
+    cudaStream_t s = nullptr;
+    cudaEvent_t f = nullptr, j = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return false;
+    if (cudaEventCreateWithFlags(&f, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&j, cudaEventDisableTiming) != cudaSuccess) {
+      if (f) cudaEventDestroy(f);
+      cudaStreamDestroy(s);
+      return false;
+    }
+    ws.side = s;
+    ws.fork = f;
+    ws.join = j;
+  }
+  *side = ws.side;
+  *fork = ws.fork;
+  *join = ws.join;
+  return true;
 }
 
 // Tensor maps over the caller's buffers (encoded per call: they hold the
@@ -292,6 +326,21 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   const int G = choose_cluster(prm.batch, span_pages, num_sms);
   IndexerParams params = prm;
   int launches = 1;
+  auto launch = [&](const IndexerParams& pp, int64_t rows, int g, cudaStream_t st) -> int {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(g * rows), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(g);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+  };
   // More clusters than fit at once: serve the longest rows first so that no
   // long row starts in the last wave.
   if (prm.batch > 1 && static_cast<int64_t>(G) * prm.batch > 2 * num_sms) {
@@ -301,21 +350,30 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
       if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
       params.order = order;
       launches = 2;
+      // When the short rows fit at two CTAs each, run everything in one
+      // wave: the R longest rows at G CTAs and the rest at 2, as two
+      // launches on two streams (DSA_TOPK_SPLIT=0 turns this off).
+      constexpr int kGLow = 2;
+      const int64_t R = (2 * static_cast<int64_t>(num_sms) - kGLow * prm.batch) / (G - kGLow > 0 ? G - kGLow : 1);
+      const char* split_env = std::getenv("DSA_TOPK_SPLIT");
+      cudaStream_t side = nullptr;
+      cudaEvent_t fork = nullptr, join = nullptr;
+      if (G > kGLow && R >= 1 && R < prm.batch && !(split_env && split_env[0] == '0') &&
+          side_stream(stream, &side, &fork, &join)) {
+        if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
+          return DSA_ERR_CUDA;
+        IndexerParams lo = params;
+        lo.order = order + R;
+        if ((rc = launch(params, R, G, stream)) != DSA_OK) return rc;
+        if ((rc = launch(lo, prm.batch - R, kGLow, side)) != DSA_OK) return rc;
+        if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
+          return DSA_ERR_CUDA;
+        t_last_launches = 3;
+        return DSA_OK;
+      }
     }
   }
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(G * static_cast<int64_t>(prm.batch)), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(G);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, params) != cudaSuccess) return DSA_ERR_CUDA;
+  if ((rc = launch(params, prm.batch, G, stream)) != DSA_OK) return rc;
   t_last_launches = launches;
   return DSA_OK;
 }
@@ -423,8 +481,9 @@ int launch_segmented(const void* q, const void* kcache, const float* w, const In
     scfg.numAttrs = pdl ? 1 : 0;
     if (cudaLaunchKernelEx(&scfg, segment_stream_kernel, tk, ts, tq, tw, sp) != cudaSuccess) return DSA_ERR_CUDA;
   }
-  // Merge: clusters of Gm CTAs per row, enough to cover the GPU about twice.
-  int64_t gm = (2 * num_sms + B - 1) / B;
+  // Merge: clusters of Gm CTAs per row, as many as fit in one wave of two
+  // CTAs per SM (a second wave would add a whole merge to the critical path).
+  int64_t gm = (2 * num_sms) / B;
   if (gm > s_max) gm = s_max;
   if (gm > 8) gm = 8;
   if (gm < 1) gm = 1;
@@ -481,9 +540,21 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
   IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
-  // DSA_TOPK_PATH=cluster forces the one-launch cluster kernel (tests).
-  const char* path = std::getenv("DSA_TOPK_PATH");
-  if (!(path && std::strcmp(path, "cluster") == 0)) {
+  // Path: the segment-scheduled kernels when the K pool is larger than L2
+  // (the rows stream from HBM and the load balance of equal segments pays
+  // for the extra merge launch), else the cluster kernel (pool L2-resident:
+  // compute-bound, or too little work to amortise three launches).
+  // DSA_TOPK_PATH=cluster|segmented forces one (tests, tuning).
+  int num_sms = 0;
+  int64_t l2 = 0;
+  rc = prepare_device(&num_sms, &l2);
+  if (rc != DSA_OK) return rc;
+  bool segmented = num_pages * static_cast<int64_t>(kPageBytes) > l2;
+  if (const char* path = std::getenv("DSA_TOPK_PATH")) {
+    if (std::strcmp(path, "cluster") == 0) segmented = false;
+    if (std::strcmp(path, "segmented") == 0) segmented = true;
+  }
+  if (segmented) {
     bool taken = false;
     rc = launch_segmented(q, k_cache, weights, p, static_cast<cudaStream_t>(stream), &taken);
     if (rc != DSA_OK || taken) return rc;

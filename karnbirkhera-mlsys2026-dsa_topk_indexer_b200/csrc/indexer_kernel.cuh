@@ -262,28 +262,23 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   if (rank != 0 || tid >= 256) return;
 
   // ---- CTA 0, threads 0..255: order the survivors and emit ----
-  uint64_t* fin = reinterpret_cast<uint64_t*>(smem + L::kFinal);
+  // Every survivor lies in [T, cluster max] (T = 0 when all were taken).
+  const uint64_t kmin = T > mm[0] ? T : static_cast<uint64_t>(mm[0]);
+  const uint64_t kmax = mm[1];
   RankScratch sc;
   sc.tmp = reinterpret_cast<uint64_t*>(smem + L::kRankTmp);
   sc.cnt = reinterpret_cast<uint32_t*>(smem + L::kRankCnt);
   sc.start = sc.cnt + 2048;
   sc.fill = sc.start + 2048;
   sc.wsum = misc_nv + kMiscWsum;
-  sc.mm = mm;
-  block_rank_order<kBarLow>(fin, nsel, sc);
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    const uint32_t i = static_cast<uint32_t>(tid * 8 + r);
-    const bool live = i < nsel;
-    const uint64_t key = live ? fin[i] : 0ull;
-    const uint32_t pos = key_pos(key);
-    const int64_t o = static_cast<int64_t>(b) * kTopK + i;
-    if (kMode == kModeTopK) {
-      p.out[o] = live ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
-    } else {
-      p.cand_scores[o] = live ? ordered_to_float(static_cast<uint32_t>(key >> 32)) : -__int_as_float(0x7f800000);
-      p.cand_pos[o] = live ? static_cast<int32_t>(pos) : -1;
-    }
+  const uint64_t* fin = reinterpret_cast<const uint64_t*>(smem + L::kFinal);
+  const int64_t o = static_cast<int64_t>(b) * kTopK;
+  if (kMode == kModeTopK) {
+    EmitSlots e{p.out + o, bt_row};
+    block_rank_emit<kBarLow>(fin, nsel, kmin, kmax, sc, e);
+  } else {
+    EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
+    block_rank_emit<kBarLow>(fin, nsel, kmin, kmax, sc, e);
   }
 }
 

@@ -292,107 +292,186 @@ __device__ __forceinline__ void warp_range(uint32_t n, int gw, int NW, uint32_t*
   *hi = a + chunk < n ? a + chunk : n;
 }
 
-// Shared-memory scratch of block_rank_order (all arrays 2048 long).
+// Shared-memory scratch of block_rank_emit: tmp (2048 keys) and three arrays
+// of 4096 16-bit bucket fields packed two per word (2048 words each).
 struct RankScratch {
   uint64_t* tmp;
   uint32_t* cnt;
   uint32_t* start;
   uint32_t* fill;
-  uint32_t* wsum;           // 8 words
-  unsigned long long* mm;   // 2 words
+  uint32_t* wsum;  // 8 words
 };
 
-// Puts the n <= 2048 unique keys of keys[] in descending order, in place.
-// 256 threads (t = 0..255) synchronised by barrier BAR. Instead of a sorting
-// network (which on 256 threads is bound by shared-memory traffic or shuffle
-// latency at tens of thousands of cycles for 2048 64-bit keys), keys are
-// counted into 2048 buckets, scattered bucket by bucket, and each key's final
-// rank is the number of keys in higher buckets plus the number of larger keys
-// in its own bucket. Exact for any input as long as the bucket of a key is a
-// non-decreasing function of the key.
+constexpr int kRankBuckets = 4096;
+
+__device__ __forceinline__ uint32_t half16(const uint32_t* a, uint32_t d) {
+  return (a[d >> 1] >> ((d & 1u) * 16u)) & 0xFFFFu;
+}
+
+// Ranks the n <= 2048 unique keys of keys[] in descending order and hands
+// every key to the emitter with its rank: emit.load(key) fetches what is
+// written for the key (issued for all of a thread's keys before any store),
+// emit.store(rank, value) writes it, emit.pad(i) fills ranks n..2047.
+// 256 threads (t = 0..255) synchronised by barrier BAR; kmin <= every key <=
+// kmax. Instead of a sorting network (which on 256 threads is bound by
+// shared-memory traffic or shuffle latency at tens of thousands of cycles for
+// 2048 64-bit keys), keys are counted into 4096 buckets, scattered bucket by
+// bucket, and each key's rank is the number of keys in higher buckets plus
+// the number of larger keys in its own bucket. Exact for any input as long
+// as the bucket of a key is a non-decreasing function of the key. The cost
+// is dominated by the in-bucket comparisons, so buckets are many (16-bit
+// counters, two per word) and evenly used:
 //
-// Buckets split the score range [min, max] of the keys linearly, so the cost
-// stays a handful of comparisons per key however the range sits relative to
-// powers of two (a window of key bits would put the whole set into one or
-// two buckets whenever the range crosses one, since the first differing bits
-// are then exponent bits). When the score range is empty or not finite the
-// 11 key bits below the keys' common prefix are used instead (equal scores
-// then spread by position).
-template <int BAR>
-__device__ __noinline__ void block_rank_order(uint64_t* keys, uint32_t n, const RankScratch sc) {
+// they split the score range [score(kmin), score(kmax)] linearly, so a bucket
+// holds a few keys however the range sits relative to powers of two (a window
+// of key bits would put the whole set into one or two buckets whenever the
+// range crosses one, since the first differing bits are then exponent bits).
+// When the score range is empty or not finite the 12 key bits below the
+// common prefix of kmin and kmax are used instead (equal scores then spread
+// by position).
+template <int BAR, class Emit>
+__device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n, uint64_t kmin, uint64_t kmax,
+                                                const RankScratch sc, Emit& emit) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  if (t == 0) {
-    sc.mm[0] = ~0ull;
-    sc.mm[1] = 0ull;
+  {  // clear cnt and fill (2048 words each) with 16-byte stores
+    uint4* c4 = reinterpret_cast<uint4*>(sc.cnt);
+    uint4* f4 = reinterpret_cast<uint4*>(sc.fill);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      c4[t + 256 * j] = z;
+      f4[t + 256 * j] = z;
+    }
   }
-  for (int i = t; i < 2048; i += 256) {
-    sc.cnt[i] = 0u;
-    sc.fill[i] = 0u;
-  }
-  group_sync<256, BAR>();
-  group_minmax<256, BAR>(keys, n, sc.mm, t);
-  const uint64_t kmin = sc.mm[0], kmax = sc.mm[1];
   const float smin = ordered_to_float(static_cast<uint32_t>(kmin >> 32));
   const float smax = ordered_to_float(static_cast<uint32_t>(kmax >> 32));
   const float range = smax - smin;
-  const float scale = 2048.f / range;
+  const float scale = static_cast<float>(kRankBuckets) / range;
   const bool lin = isfinite(smin) && isfinite(smax) && range > 0.f && isfinite(range) && isfinite(scale);
   const uint64_t x = kmin ^ kmax;
   const int top = x ? __clzll(static_cast<long long>(x)) : 64;
-  const int shift = (64 - top - 11) > 0 ? (64 - top - 11) : 0;
+  const int shift = (64 - top - 12) > 0 ? (64 - top - 12) : 0;
   auto bucket = [&](uint64_t k) -> uint32_t {
     if (lin) {
       const float f = (ordered_to_float(static_cast<uint32_t>(k >> 32)) - smin) * scale;
-      return f >= 2047.f ? 2047u : static_cast<uint32_t>(f);
+      return f >= static_cast<float>(kRankBuckets - 1) ? static_cast<uint32_t>(kRankBuckets - 1)
+                                                        : static_cast<uint32_t>(f);
     }
-    return static_cast<uint32_t>(k >> shift) & 2047u;
+    return static_cast<uint32_t>(k >> shift) & static_cast<uint32_t>(kRankBuckets - 1);
   };
-  for (uint32_t i = t; i < n; i += 256) atomicAdd(&sc.cnt[bucket(keys[i])], 1u);
-  group_sync<256, BAR>();
-  // Exclusive scan in descending bucket order; thread t owns buckets
-  // 2047-8t down to 2040-8t.
-  uint32_t c[8], tot = 0;
+  uint64_t k[8];
+  uint32_t d[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    c[j] = sc.cnt[2047 - 8 * t - j];
-    tot += c[j];
+    const uint32_t i = t + 256 * j;
+    k[j] = i < n ? keys[i] : 0ull;
+    d[j] = bucket(k[j]);
   }
-  uint32_t incl = tot;
+  group_sync<256, BAR>();
 #pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
-    if (lane >= off) incl += v;
-  }
-  if (lane == 31) sc.wsum[w] = incl;
+  for (int j = 0; j < 8; ++j)
+    if (t + 256 * j < n) atomicAdd(&sc.cnt[d[j] >> 1], 1u << ((d[j] & 1u) * 16u));
   group_sync<256, BAR>();
-  uint32_t base = incl - tot;
-  for (int k = 0; k < w; ++k) base += sc.wsum[k];
+  // Exclusive scan in descending bucket order; thread t owns words
+  // 2047-8t down to 2040-8t, i.e. buckets 4095-16t down to 4080-16t (in a
+  // word the odd bucket, high half, comes first).
+  {
+    uint32_t c[8], tot = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    sc.start[2047 - 8 * t - j] = base;
-    base += c[j];
-  }
-  group_sync<256, BAR>();
-  for (uint32_t i = t; i < n; i += 256) {
-    const uint64_t k = keys[i];
-    const uint32_t d = bucket(k);
-    sc.tmp[sc.start[d] + atomicAdd(&sc.fill[d], 1u)] = k;
-  }
-  group_sync<256, BAR>();
-  for (uint32_t i = t; i < n; i += 256) {
-    const uint64_t k = sc.tmp[i];
-    const uint32_t d = bucket(k);
-    const uint32_t b0 = sc.start[d], b1 = b0 + sc.cnt[d];
-    uint32_t r0 = 0, r1 = 0;
-    uint32_t q = b0;
-    for (; q + 1 < b1; q += 2) {
-      r0 += (sc.tmp[q] > k) ? 1u : 0u;
-      r1 += (sc.tmp[q + 1] > k) ? 1u : 0u;
+    for (int j = 0; j < 8; ++j) {
+      c[j] = sc.cnt[2047 - 8 * t - j];
+      tot += (c[j] >> 16) + (c[j] & 0xFFFFu);
     }
-    if (q < b1) r0 += (sc.tmp[q] > k) ? 1u : 0u;
-    keys[b0 + r0 + r1] = k;
+    uint32_t incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    if (lane == 31) sc.wsum[w] = incl;
+    group_sync<256, BAR>();
+    uint32_t base = incl - tot;
+    for (int q = 0; q < w; ++q) base += sc.wsum[q];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t hi = base;
+      const uint32_t lo = base + (c[j] >> 16);
+      sc.start[2047 - 8 * t - j] = (hi << 16) | lo;
+      base = lo + (c[j] & 0xFFFFu);
+    }
   }
   group_sync<256, BAR>();
+  {  // scatter: all slot atomics first, then the stores that need them
+    uint32_t slot[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t sh = (d[j] & 1u) * 16u;
+      slot[j] = (t + 256 * j < n)
+                    ? half16(sc.start, d[j]) + ((atomicAdd(&sc.fill[d[j] >> 1], 1u << sh) >> sh) & 0xFFFFu)
+                    : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (t + 256 * j < n) sc.tmp[slot[j]] = k[j];
+  }
+  group_sync<256, BAR>();
+  uint32_t r[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t i = t + 256 * j;
+    r[j] = 0u;
+    k[j] = 0ull;
+    if (i < n) {
+      const uint64_t key = sc.tmp[i];
+      const uint32_t dd = bucket(key);
+      const uint32_t b0 = half16(sc.start, dd), b1 = b0 + half16(sc.cnt, dd);
+      uint32_t r0 = 0, r1 = 0, q = b0;
+      for (; q + 1 < b1; q += 2) {
+        r0 += (sc.tmp[q] > key) ? 1u : 0u;
+        r1 += (sc.tmp[q + 1] > key) ? 1u : 0u;
+      }
+      if (q < b1) r0 += (sc.tmp[q] > key) ? 1u : 0u;
+      r[j] = b0 + r0 + r1;
+      k[j] = key;
+    }
+  }
+  typename Emit::Value v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (t + 256 * j < n) v[j] = emit.load(k[j]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (t + 256 * j < n) emit.store(r[j], v[j]);
+  for (uint32_t i = n + t; i < static_cast<uint32_t>(kTopK); i += 256) emit.pad(i);
 }
+
+// Emitters: the top-K physical slots of one row, or its (score, logical
+// position) candidate list.
+struct EmitSlots {
+  using Value = int32_t;
+  int32_t* out;           // row of 2048
+  const int32_t* bt_row;  // block-table row
+  __device__ __forceinline__ int32_t load(uint64_t key) const {
+    const uint32_t pos = key_pos(key);
+    return bt_row[pos >> 6] * 64 + static_cast<int32_t>(pos & 63u);
+  }
+  __device__ __forceinline__ void store(uint32_t r, int32_t v) const { out[r] = v; }
+  __device__ __forceinline__ void pad(uint32_t i) const { out[i] = -1; }
+};
+
+struct EmitCandidates {
+  using Value = uint64_t;
+  float* scores;  // row of 2048
+  int32_t* pos;   // row of 2048
+  __device__ __forceinline__ uint64_t load(uint64_t key) const { return key; }
+  __device__ __forceinline__ void store(uint32_t r, uint64_t key) const {
+    scores[r] = ordered_to_float(static_cast<uint32_t>(key >> 32));
+    pos[r] = static_cast<int32_t>(key_pos(key));
+  }
+  __device__ __forceinline__ void pad(uint32_t i) const {
+    scores[i] = -__int_as_float(0x7f800000);
+    pos[i] = -1;
+  }
+};
 
 }  // namespace dsa

@@ -251,6 +251,7 @@ def test_segmented_path_segment_and_merge_sizes(pkg, seg, gm, monkeypatch):
     """The segment-scheduled path for several segment lengths and merge
     cluster sizes: rows shorter than, equal to and much longer than one
     segment, an empty row, odd tile counts."""
+    monkeypatch.setenv("DSA_TOPK_PATH", "segmented")
     monkeypatch.setenv("DSA_TOPK_SEG", str(seg))
     monkeypatch.setenv("DSA_TOPK_MERGE_CLUSTER", str(gm))
     w = workloads().custom([0, 64, 130, 2049, 4097, 12345, 33000, 300], seed=23)
@@ -262,9 +263,33 @@ def test_segmented_merge_many_short_lists(pkg, gm, monkeypatch):
     """Segments of two tiles on rows of up to 131072 keys: a merge CTA gets
     more lists than it has threads and more keys than its buffer holds, so
     it takes several rounds of list copies with exact cuts in between."""
+    monkeypatch.setenv("DSA_TOPK_PATH", "segmented")
     monkeypatch.setenv("DSA_TOPK_SEG", "2")
     monkeypatch.setenv("DSA_TOPK_MERGE_CLUSTER", str(gm))
     w = workloads().custom([131072, 65543, 1, 20000], seed=29)
+    assert_parity(pkg, w)
+
+
+@pytest.mark.parametrize("cfg", [0, 1, 3])
+def test_segmented_path_configs(pkg, cfg, monkeypatch):
+    """The segment-scheduled path forced on workloads whose pool fits in L2
+    (where the cluster kernel is the default), prefill rows included."""
+    monkeypatch.setenv("DSA_TOPK_PATH", "segmented")
+    w = workloads().config(cfg)
+    if cfg == 3:
+        w = _rows(w, list(range(0, 8192, 41)))
+    assert_parity(pkg, w)
+
+
+@pytest.mark.parametrize("split", ["0", "1"])
+def test_cluster_two_class_launch(pkg, split, monkeypatch):
+    """Cluster path on a batch that needs more clusters than fit at once:
+    the longest rows at the default cluster size and the rest at two CTAs
+    each, launched concurrently on two streams (split=1), or all rows at one
+    size in longest-first order (split=0)."""
+    monkeypatch.setenv("DSA_TOPK_PATH", "cluster")
+    monkeypatch.setenv("DSA_TOPK_SPLIT", split)
+    w = workloads().custom([32768, 600, 0, 17000, 2049, 9000, 100, 24000] * 8, seed=31)
     assert_parity(pkg, w)
 
 
