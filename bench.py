@@ -36,13 +36,19 @@ def peaks():
     return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
-def traffic_per_launch(config):
-    """DRAM bytes per launch of the indexer kernel from the committed ncu
-    summary (profiles/traffic.json), or None."""
+def traffic_per_launch(config, kernel):
+    """DRAM bytes per launch of `kernel` on `config` from the committed ncu
+    summaries (profiles/traffic.json), or None."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if not os.path.exists(p):
         return None
-    return json.load(open(p)).get(f"cfg{config}")
+    return json.load(open(p)).get(f"cfg{config}:{kernel}")
+
+
+DOMINANT = {"segmented": "dsa::segment_stream_kernel", "cluster": "dsa::indexer_kernel<0>",
+            "cluster-split": "dsa::indexer_kernel<0>"}
+PREFILL_CONFIGS = (3, 4)
+FLOP_PER_KEY = 64 * 128 * 2  # one query row against one key: 64 heads x 128-dim dot products
 
 
 class ClockSampler:
@@ -125,6 +131,8 @@ def main():
     ap.add_argument("--config", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch-scale", type=float, default=1.0,
+                    help="profiling only: run the config with its batch scaled down (ncu captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -146,7 +154,7 @@ def main():
     pkg = importlib.import_module(PKG_NAME)
     pkg._lib.load()
 
-    w = wl.config(args.config, device=dev, seed=args.config + 1000 * rank)
+    w = wl.config(args.config, device=dev, seed=args.config + 1000 * rank, scale_batch=args.batch_scale)
     B = w.batch
     out = torch.empty((B, 2048), dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
@@ -198,6 +206,20 @@ def main():
     ms = sum(step_ms) / len(step_ms)
     status = pkg.device_status(local, clear=True)
 
+    # ---------------- dominant-kernel time (roofline) ----------------
+    # The library brackets the call's dominant kernel with CUDA events on
+    # the launching stream; a separate pass of the same K steps (the events
+    # keep the bracketed kernel from overlapping its neighbours).
+    pkg.set_kernel_timing(True)
+    kms = []
+    for i in range(args.steps):
+        flush.zero_()
+        call()
+        kms.append(pkg.last_kernel_ms())
+    pkg.set_kernel_timing(False)
+    path = pkg.last_path()
+    kernel_ms = sum(kms) / len(kms)
+
     # ---------------- end-to-end region (host buffers) ----------------
     h_q = w.q.view(torch.uint8).cpu().pin_memory()
     h_w = w.weights.cpu().pin_memory()
@@ -236,12 +258,12 @@ def main():
     assert torch.equal(h_out, out.cpu()), "e2e output mismatch"
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, e2e_ms, kernel_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max = float(t[0]), float(t[1])
+    ms_max, e2e_max, kms_max = float(t[0]), float(t[1]), float(t[2])
     kbytes = w.kcache_bytes()
-    hbm, _, peak_src = peaks()
+    hbm, bf16, peak_src = peaks()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -251,23 +273,37 @@ def main():
                          f"(oracle/reference_torch.py), {dt:.2f} s"}
 
     if rank == 0:
-        achieved = kbytes / (ms_max * 1e-3) / 1e9
-        tr = traffic_per_launch(args.config)
+        kernel = DOMINANT.get(path, path)
+        tr = traffic_per_launch(args.config, kernel)
+        if args.config in PREFILL_CONFIGS:
+            # K is L2-resident (one sequence): the contraction on the tensor
+            # cores bounds the kernel. B200's dense fp8 rate is twice bf16.
+            flops = w.visible_keys() * FLOP_PER_KEY
+            achieved = flops / (kms_max * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16, "unit": "TFLOP/s",
+                    "frac": achieved / (2 * bf16), "traffic": tr,
+                    "peak_source": f"2 x {peak_src} bf16 dense (fp8 dense rate)",
+                    "algorithmic_flops_per_launch": flops}
+        else:
+            achieved = kbytes / (kms_max * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                    "traffic": tr, "peak_source": peak_src, "algorithmic_bytes_per_launch": kbytes}
+        roof.update({"kernel": kernel, "kernel_ms": kms_max, "schedule": path,
+                     "kernel_timing": "CUDA events on the launching stream around the kernel, "
+                                      "separate pass of the same steps"})
         line = {
             "metric": METRIC, "value": B * world / (ms_max * 1e-3), "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": w.name, "batch_per_gpu": B, "global_batch": B * world,
+            "config": {"workload": w.name + ("" if args.batch_scale == 1.0 else f" (batch x{args.batch_scale})"),
+                       "batch_per_gpu": B, "global_batch": B * world,
                        "visible_keys_per_gpu": w.visible_keys(), "max_pages": w.max_pages,
                        "pool_pages": w.num_pages, "parallelism": f"request-sharded x{world}",
                        "l2": "flushed (256 MB write) before every timed step"},
             "e2e": {"value": B * world / (e2e_max * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max,
                     "kcache": "resident in HBM (persistent serving state)"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": tr, "peak_source": peak_src,
-                         "algorithmic_bytes_per_launch": kbytes,
-                         "kernel": "dsa::indexer_kernel<0>"},
+            "roofline": roof,
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "status_word": status,

@@ -135,6 +135,23 @@ DSA_API const char* dsa_topk_indexer_error_string(int code);
 /* Number of kernel launches the last successful call on this host thread made. */
 DSA_API int dsa_topk_indexer_last_launch_count(void);
 
+/* Schedule the last successful top-K call on this host thread took:
+ * "segmented" (plan, persistent stream kernel, cluster merge), "cluster"
+ * (one cluster kernel, optionally after the longest-first plan) or
+ * "cluster-split" (two concurrent cluster kernels). */
+DSA_API const char* dsa_topk_indexer_last_path(void);
+
+/* Per-kernel timing for profiling, off by default. While on, every call
+ * records CUDA events on its stream around its dominant kernel (the stream
+ * kernel of the segmented schedule, the cluster kernel or kernels otherwise)
+ * and dsa_topk_indexer_kernel_ms waits for the last call on this host thread
+ * and returns that kernel's device time in milliseconds. The events keep the
+ * bracketed launch from overlapping its neighbours, so timed calls are not
+ * the fastest; calls made while their stream is being captured are not
+ * timed (kernel_ms then returns DSA_ERR_INVALID_ARG). */
+DSA_API int dsa_topk_indexer_set_timing(int on);
+DSA_API int dsa_topk_indexer_kernel_ms(float* ms);
+
 #ifdef __cplusplus
 }
 #endif

@@ -169,3 +169,25 @@ def device_status(device=0, clear=True):
 
 def last_launch_count():
     return _lib.load().dsa_topk_indexer_last_launch_count()
+
+
+def last_path():
+    """Schedule of the last top-K call on this thread: "segmented", "cluster"
+    or "cluster-split"."""
+    return _lib.load().dsa_topk_indexer_last_path().decode()
+
+
+def set_kernel_timing(on):
+    """Turns per-kernel timing events on or off (profiling only)."""
+    _lib.load().dsa_topk_indexer_set_timing(1 if on else 0)
+
+
+def last_kernel_ms():
+    """Device time of the dominant kernel of the last call on this thread
+    (timing must have been on for it); waits for that call."""
+    import ctypes
+    v = ctypes.c_float(0.0)
+    rc = _lib.load().dsa_topk_indexer_kernel_ms(ctypes.byref(v))
+    if rc != 0:
+        raise RuntimeError(_lib.load().dsa_topk_indexer_error_string(rc).decode())
+    return float(v.value)

@@ -29,6 +29,9 @@ SIGNATURES = [
     ("dsa_topk_indexer_status", _I32, [_I32, ctypes.POINTER(ctypes.c_uint32), _I32]),
     ("dsa_topk_indexer_error_string", ctypes.c_char_p, [_I32]),
     ("dsa_topk_indexer_last_launch_count", _I32, []),
+    ("dsa_topk_indexer_last_path", ctypes.c_char_p, []),
+    ("dsa_topk_indexer_set_timing", _I32, [_I32]),
+    ("dsa_topk_indexer_kernel_ms", _I32, [ctypes.POINTER(ctypes.c_float)]),
 ]
 
 _lib = None

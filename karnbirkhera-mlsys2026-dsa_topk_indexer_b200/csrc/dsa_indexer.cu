@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -111,6 +112,32 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 thread_local int t_last_launches = 0;
+thread_local const char* t_last_path = "";
+
+// Optional per-kernel timing (dsa_topk_indexer_set_timing).
+std::atomic<int> g_timing{0};
+thread_local cudaEvent_t t_ev_begin = nullptr, t_ev_end = nullptr;
+thread_local bool t_timed = false;
+
+// Brackets the dominant kernel of a call with timing events when timing is
+// on and the stream is not being captured.
+struct KernelTimer {
+  cudaStream_t stream;
+  bool on = false;
+  explicit KernelTimer(cudaStream_t s) : stream(s) {
+    t_timed = false;
+    if (!g_timing.load()) return;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return;
+    if (!t_ev_begin && (cudaEventCreate(&t_ev_begin) != cudaSuccess || cudaEventCreate(&t_ev_end) != cudaSuccess))
+      return;
+    on = cudaEventRecord(t_ev_begin, s) == cudaSuccess;
+  }
+  void stop() {
+    if (on && cudaEventRecord(t_ev_end, stream) == cudaSuccess) t_timed = true;
+    on = false;
+  }
+};
 
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
@@ -360,6 +387,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
       cudaEvent_t fork = nullptr, join = nullptr;
       if (G > kGLow && R >= 1 && R < prm.batch && !(split_env && split_env[0] == '0') &&
           side_stream(stream, &side, &fork, &join)) {
+        KernelTimer timer(stream);
         if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
         IndexerParams lo = params;
@@ -368,13 +396,18 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
         if ((rc = launch(lo, prm.batch - R, kGLow, side)) != DSA_OK) return rc;
         if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
+        timer.stop();
         t_last_launches = 3;
+        t_last_path = "cluster-split";
         return DSA_OK;
       }
     }
   }
+  KernelTimer timer(stream);
   if ((rc = launch(params, prm.batch, G, stream)) != DSA_OK) return rc;
+  timer.stop();
   t_last_launches = launches;
+  t_last_path = "cluster";
   return DSA_OK;
 }
 
@@ -479,7 +512,9 @@ int launch_segmented(const void* q, const void* kcache, const float* w, const In
     sattr[0].val.programmaticStreamSerializationAllowed = 1;
     scfg.attrs = sattr;
     scfg.numAttrs = pdl ? 1 : 0;
+    KernelTimer timer(stream);
     if (cudaLaunchKernelEx(&scfg, segment_stream_kernel, tk, ts, tq, tw, sp) != cudaSuccess) return DSA_ERR_CUDA;
+    timer.stop();
   }
   // Merge: clusters of Gm CTAs per row, as many as fit in one wave of two
   // CTAs per SM (a second wave would add a whole merge to the critical path).
@@ -510,6 +545,7 @@ int launch_segmented(const void* q, const void* kcache, const float* w, const In
   cfg.numAttrs = pdl ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, segment_merge_kernel, mp, prm) != cudaSuccess) return DSA_ERR_CUDA;
   t_last_launches = 3;
+  t_last_path = "segmented";
   *taken = true;
   return DSA_OK;
 }
@@ -740,3 +776,16 @@ extern "C" const char* dsa_topk_indexer_error_string(int code) {
 }
 
 extern "C" int dsa_topk_indexer_last_launch_count(void) { return t_last_launches; }
+
+extern "C" const char* dsa_topk_indexer_last_path(void) { return t_last_path; }
+
+extern "C" int dsa_topk_indexer_set_timing(int on) {
+  g_timing.store(on ? 1 : 0);
+  return DSA_OK;
+}
+
+extern "C" int dsa_topk_indexer_kernel_ms(float* ms) {
+  if (!ms || !t_timed) return DSA_ERR_INVALID_ARG;
+  if (cudaEventSynchronize(t_ev_end) != cudaSuccess) return DSA_ERR_CUDA;
+  return cudaEventElapsedTime(ms, t_ev_begin, t_ev_end) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
