@@ -28,8 +28,8 @@ namespace dsa {
 constexpr int kMergeThreads = 256;
 constexpr int kMergeCap = 4096;
 // cand keys, histogram, misc words (count, digit scan, min/max, scan scratch),
-// then the ordering scratch (bucket counts, starts, fill).
-constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 128 + 3 * 2048 * 4;
+// then the ordering scratch (bucket counts, starts, fill, bucket of each slot).
+constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 128 + 3 * 2048 * 4 + kTopK * 2;
 
 __global__ void __launch_bounds__(kMergeThreads, 1)
     merge_kernel(const float* __restrict__ cand_scores, const int32_t* __restrict__ cand_pos, int nparts,
@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
   sc.cnt = rank_cnt;
   sc.start = rank_cnt + 2048;
   sc.fill = rank_cnt + 4096;
+  sc.tmpd = reinterpret_cast<uint16_t*>(rank_cnt + 6144);
   sc.wsum = misc + 16;
   EmitSlots e{out + static_cast<int64_t>(b) * kTopK, block_table + static_cast<int64_t>(b) * max_pages};
   block_rank_emit<0>(cand, nsel, mm[0], mm[1], sc, e);
@@ -577,15 +578,17 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
   IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
   // Path: the segment-scheduled kernels when the K pool is larger than L2
-  // (the rows stream from HBM and the load balance of equal segments pays
-  // for the extra merge launch), else the cluster kernel (pool L2-resident:
-  // compute-bound, or too little work to amortise three launches).
+  // and the batch is larger than the SM count (rows stream from HBM and the
+  // load balance of equal segments pays for the extra merge launch; measured
+  // on B200 with B=512). Otherwise the cluster kernel: pool L2-resident
+  // (compute-bound), or few enough rows that all clusters fit in one wave
+  // with the two-class launch (B=64: 49 us against 53 us segmented).
   // DSA_TOPK_PATH=cluster|segmented forces one (tests, tuning).
   int num_sms = 0;
   int64_t l2 = 0;
   rc = prepare_device(&num_sms, &l2);
   if (rc != DSA_OK) return rc;
-  bool segmented = num_pages * static_cast<int64_t>(kPageBytes) > l2;
+  bool segmented = num_pages * static_cast<int64_t>(kPageBytes) > l2 && batch > num_sms;
   if (const char* path = std::getenv("DSA_TOPK_PATH")) {
     if (std::strcmp(path, "cluster") == 0) segmented = false;
     if (std::strcmp(path, "segmented") == 0) segmented = true;

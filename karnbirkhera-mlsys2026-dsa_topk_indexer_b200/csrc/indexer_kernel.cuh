@@ -68,7 +68,8 @@ constexpr int kSmemBytes = kSmemUsed + 1024;              // alignment slack
 constexpr int kOffFinal = kOffK;                          // 2048 x 8
 constexpr int kOffRankTmp = kOffFinal + kTopK * 8;        // 2048 x 8
 constexpr int kOffRankCnt = kOffRankTmp + kTopK * 8;      // 3 x 2048 x 4 (cnt, start, fill)
-static_assert(kOffRankCnt + 3 * 2048 * 4 <= kOffQ, "ordering scratch must fit in the K ring");
+constexpr int kOffRankD = kOffRankCnt + 3 * 2048 * 4;     // 2048 x 2 (bucket of each tmp slot)
+static_assert(kOffRankD + kTopK * 2 <= kOffQ, "ordering scratch must fit in the K ring");
 static_assert(kStages * 16384 % 1024 == 0, "K tiles must stay 1024-aligned");
 static_assert((2 * kStages + 2 * kTmemBufs + 1) * 8 <= 256, "barrier area");
 
@@ -150,7 +151,7 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
 // cluster barrier, when `Cand` is dead.
 struct StreamSelectLayout {
   static constexpr int kCand = kOffCand, kHist = kOffHist, kTot = kOffTot, kMisc = kOffMisc;
-  static constexpr int kFinal = kOffFinal, kRankTmp = kOffRankTmp, kRankCnt = kOffRankCnt;
+  static constexpr int kFinal = kOffFinal, kRankTmp = kOffRankTmp, kRankCnt = kOffRankCnt, kRankD = kOffRankD;
 };
 
 template <int kMode, class L>
@@ -267,6 +268,7 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   const uint64_t kmax = mm[1];
   RankScratch sc;
   sc.tmp = reinterpret_cast<uint64_t*>(smem + L::kRankTmp);
+  sc.tmpd = reinterpret_cast<uint16_t*>(smem + L::kRankD);
   sc.cnt = reinterpret_cast<uint32_t*>(smem + L::kRankCnt);
   sc.start = sc.cnt + 2048;
   sc.fill = sc.start + 2048;

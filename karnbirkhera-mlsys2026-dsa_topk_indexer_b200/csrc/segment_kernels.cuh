@@ -554,12 +554,13 @@ constexpr int kM_OffWsum = kM_OffSegOff + kThreads * 4;       // 16 x 4
 constexpr int kM_OffMisc = kM_OffWsum + 64;                   // misc words
 constexpr int kM_SmemBytes = kM_OffMisc + 128 + 1024;
 static_assert(kMergeKeys >= 2 * kCap + kTopK, "a cut buffer must take two more lists");
-static_assert(kTopK * 8 + 3 * 2048 * 4 <= kMergeKeys * 8, "ordering scratch must fit in the candidate buffer");
+static_assert(kTopK * 8 + 3 * 2048 * 4 + kTopK * 2 <= kMergeKeys * 8, "ordering scratch must fit in the candidate buffer");
 static_assert(2 * (kM_SmemBytes + 1024) <= 233472, "two merge CTAs per SM");
 
 struct MergeSelectLayout {
   static constexpr int kCand = kM_OffCand, kHist = kM_OffHist, kTot = kM_OffTot, kMisc = kM_OffMisc;
   static constexpr int kFinal = kM_OffFinal, kRankTmp = kM_OffCand, kRankCnt = kM_OffCand + kTopK * 8;
+  static constexpr int kRankD = kRankCnt + 3 * 2048 * 4;
 };
 
 // Inclusive scan of one value per thread over the CTA's kThreads threads;

@@ -292,10 +292,12 @@ __device__ __forceinline__ void warp_range(uint32_t n, int gw, int NW, uint32_t*
   *hi = a + chunk < n ? a + chunk : n;
 }
 
-// Shared-memory scratch of block_rank_emit: tmp (2048 keys) and three arrays
-// of 4096 16-bit bucket fields packed two per word (2048 words each).
+// Shared-memory scratch of block_rank_emit: tmp (2048 keys), the bucket of
+// each tmp slot (2048 x 16 bits) and three arrays of 4096 16-bit bucket
+// fields packed two per word (2048 words each).
 struct RankScratch {
   uint64_t* tmp;
+  uint16_t* tmpd;
   uint32_t* cnt;
   uint32_t* start;
   uint32_t* fill;
@@ -412,29 +414,38 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (t + 256 * j < n) sc.tmp[slot[j]] = k[j];
+      if (t + 256 * j < n) {
+        sc.tmp[slot[j]] = k[j];
+        sc.tmpd[slot[j]] = static_cast<uint16_t>(d[j]);
+      }
   }
   group_sync<256, BAR>();
-  uint32_t r[8];
+  // In-bucket ranks. First pass: the first four keys of every bucket, as
+  // straight-line code over all of a thread's keys (their load chains
+  // overlap); second pass: the rest of the rare buckets holding more.
+  uint32_t r[8], b0[8], c[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const uint32_t i = t + 256 * j;
-    r[j] = 0u;
-    k[j] = 0ull;
-    if (i < n) {
-      const uint64_t key = sc.tmp[i];
-      const uint32_t dd = bucket(key);
-      const uint32_t b0 = half16(sc.start, dd), b1 = b0 + half16(sc.cnt, dd);
-      uint32_t r0 = 0, r1 = 0, q = b0;
-      for (; q + 1 < b1; q += 2) {
-        r0 += (sc.tmp[q] > key) ? 1u : 0u;
-        r1 += (sc.tmp[q + 1] > key) ? 1u : 0u;
-      }
-      if (q < b1) r0 += (sc.tmp[q] > key) ? 1u : 0u;
-      r[j] = b0 + r0 + r1;
-      k[j] = key;
+    const bool live = i < n;
+    const uint32_t ii = live ? i : 0u;
+    k[j] = sc.tmp[ii];
+    // Slots >= n were never written (all of tmpd when n == 0): dead lanes
+    // use bucket 0, and a stored id is masked to the bucket range.
+    const uint32_t dd = live ? (static_cast<uint32_t>(sc.tmpd[ii]) & static_cast<uint32_t>(kRankBuckets - 1)) : 0u;
+    b0[j] = half16(sc.start, dd);
+    c[j] = live ? half16(sc.cnt, dd) : 0u;
+    uint32_t rr = 0;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t q = b0[j] + m;
+      rr += (static_cast<uint32_t>(m) < c[j] && sc.tmp[q < 2047u ? q : 2047u] > k[j]) ? 1u : 0u;
     }
+    r[j] = b0[j] + rr;
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    for (uint32_t q = b0[j] + 4; q < b0[j] + c[j]; ++q) r[j] += (sc.tmp[q] > k[j]) ? 1u : 0u;
   typename Emit::Value v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j)
