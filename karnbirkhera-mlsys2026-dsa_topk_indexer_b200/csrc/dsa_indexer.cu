@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kMergeThreads, 1)
   sc.tmpd = reinterpret_cast<uint16_t*>(rank_cnt + 6144);
   sc.wsum = misc + 16;
   EmitSlots e{out + static_cast<int64_t>(b) * kTopK, block_table + static_cast<int64_t>(b) * max_pages};
-  block_rank_emit<0>(cand, nsel, mm[0], mm[1], sc, e);
+  block_rank_emit<0, 8>(cand, nsel, mm[0], mm[1], sc, e);
 }
 
 // Fills a float buffer (used for the -inf background of the score rows).
@@ -577,23 +577,13 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
   IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
-  // Path: the segment-scheduled kernels when the K pool is larger than L2
-  // and the batch is larger than the SM count (rows stream from HBM and the
-  // load balance of equal segments pays for the extra merge launch; measured
-  // on B200 with B=512). Otherwise the cluster kernel: pool L2-resident
-  // (compute-bound), or few enough rows that all clusters fit in one wave
-  // with the two-class launch (B=64: 49 us against 53 us segmented).
-  // DSA_TOPK_PATH=cluster|segmented forces one (tests, tuning).
-  int num_sms = 0;
-  int64_t l2 = 0;
-  rc = prepare_device(&num_sms, &l2);
-  if (rc != DSA_OK) return rc;
-  bool segmented = num_pages * static_cast<int64_t>(kPageBytes) > l2 && batch > num_sms;
-  if (const char* path = std::getenv("DSA_TOPK_PATH")) {
-    if (std::strcmp(path, "cluster") == 0) segmented = false;
-    if (std::strcmp(path, "segmented") == 0) segmented = true;
-  }
-  if (segmented) {
+  // Path: the cluster kernel (one launch, or two concurrent ones, after the
+  // longest-first plan when the clusters take more than one wave). Measured
+  // on B200 it is at least as fast as the segment-scheduled kernels on every
+  // benchmark configuration (B=512 decode: 0.84 ms against 0.95 ms), so the
+  // segmented schedule (DSA_TOPK_PATH=segmented) is opt-in.
+  const char* path = std::getenv("DSA_TOPK_PATH");
+  if (path && std::strcmp(path, "segmented") == 0) {
     bool taken = false;
     rc = launch_segmented(q, k_cache, weights, p, static_cast<cudaStream_t>(stream), &taken);
     if (rc != DSA_OK || taken) return rc;

@@ -70,6 +70,12 @@ constexpr int kOffRankTmp = kOffFinal + kTopK * 8;        // 2048 x 8
 constexpr int kOffRankCnt = kOffRankTmp + kTopK * 8;      // 3 x 2048 x 4 (cnt, start, fill)
 constexpr int kOffRankD = kOffRankCnt + 3 * 2048 * 4;     // 2048 x 2 (bucket of each tmp slot)
 static_assert(kOffRankD + kTopK * 2 <= kOffQ, "ordering scratch must fit in the K ring");
+// One-CTA rows rank all kCap candidates in place of the cluster select; the
+// K ring then holds that ordering's scratch instead.
+constexpr int kOffSoloTmp = kOffK;                        // kCap x 8
+constexpr int kOffSoloD = kOffSoloTmp + kCap * 8;         // kCap x 2
+constexpr int kOffSoloCnt = kOffSoloD + kCap * 2;         // 3 x 2048 x 4
+static_assert(kOffSoloCnt % 16 == 0 && kOffSoloCnt + 3 * 2048 * 4 <= kOffQ, "solo ordering scratch");
 static_assert(kStages * 16384 % 1024 == 0, "K tiles must stay 1024-aligned");
 static_assert((2 * kStages + 2 * kTmemBufs + 1) * 8 <= 256, "barrier area");
 
@@ -150,6 +156,8 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
 // the ordering scratch (`RankTmp`, `RankCnt`) is only touched after the last
 // cluster barrier, when `Cand` is dead.
 struct StreamSelectLayout {
+  static constexpr bool kSolo = true;  // scratch for ranking all candidates of a one-CTA row
+  static constexpr int kSoloTmp = kOffSoloTmp, kSoloD = kOffSoloD, kSoloCnt = kOffSoloCnt;
   static constexpr int kCand = kOffCand, kHist = kOffHist, kTot = kOffTot, kMisc = kOffMisc;
   static constexpr int kFinal = kOffFinal, kRankTmp = kOffRankTmp, kRankCnt = kOffRankCnt, kRankD = kOffRankD;
 };
@@ -166,8 +174,37 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   unsigned long long* pub_mm = reinterpret_cast<unsigned long long*>(smem + L::kMisc + 4 * kMiscPubMM);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // ---- cluster-wide exact selection of the best 2048 keys ----
   const int tid = threadIdx.x;
+  if constexpr (L::kSolo) {
+    if (G == 1 && n <= static_cast<uint32_t>(kCap)) {
+      // One CTA holds every candidate of the row: rank them all and emit the
+      // best 2048 (no threshold search, exchange or second pass).
+      if (tid == 0) {
+        mm[0] = ~0ull;
+        mm[1] = 0ull;
+      }
+      __syncthreads();
+      group_minmax<kThreads, 0>(cand, n, mm, tid);
+      if (tid >= 256) return;
+      RankScratch sc;
+      sc.tmp = reinterpret_cast<uint64_t*>(smem + L::kSoloTmp);
+      sc.tmpd = reinterpret_cast<uint16_t*>(smem + L::kSoloD);
+      sc.cnt = reinterpret_cast<uint32_t*>(smem + L::kSoloCnt);
+      sc.start = sc.cnt + 2048;
+      sc.fill = sc.start + 2048;
+      sc.wsum = misc_nv + kMiscWsum;
+      const int64_t o = static_cast<int64_t>(b) * kTopK;
+      if (kMode == kModeTopK) {
+        EmitSlots e{p.out + o, bt_row};
+        block_rank_emit<kBarLow, kCap / 256>(cand, n, mm[0], mm[1], sc, e);
+      } else {
+        EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
+        block_rank_emit<kBarLow, kCap / 256>(cand, n, mm[0], mm[1], sc, e);
+      }
+      return;
+    }
+  }
+  // ---- cluster-wide exact selection of the best 2048 keys ----
   const uint32_t pub_addr = base_addr + L::kMisc + 4 * kMiscPub;
   const uint32_t pub_mm_addr = base_addr + L::kMisc + 4 * kMiscPubMM;
   if (tid == 0) {
@@ -277,10 +314,10 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   const int64_t o = static_cast<int64_t>(b) * kTopK;
   if (kMode == kModeTopK) {
     EmitSlots e{p.out + o, bt_row};
-    block_rank_emit<kBarLow>(fin, nsel, kmin, kmax, sc, e);
+    block_rank_emit<kBarLow, 8>(fin, nsel, kmin, kmax, sc, e);
   } else {
     EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
-    block_rank_emit<kBarLow>(fin, nsel, kmin, kmax, sc, e);
+    block_rank_emit<kBarLow, 8>(fin, nsel, kmin, kmax, sc, e);
   }
 }
 
@@ -537,7 +574,10 @@ __global__ void __launch_bounds__(kThreads, 2)
               mm[1] = 0ull;
             }
             ptx::named_bar(kBarEpi, kEpiThreads);
-            if (n > static_cast<uint32_t>(kTopK)) {
+            // Cut only when fewer than two tile pairs of room are left:
+            // between checks the threshold already rejects most keys, so
+            // the buffer fills slowly and most checks need no cut.
+            if (n > static_cast<uint32_t>(kCap - 4 * kTileKeys)) {
               // Cheap safe cut; the exact selection only if the cut frees
               // too little room. Keys below the cut can never reach the top
               // 2048.

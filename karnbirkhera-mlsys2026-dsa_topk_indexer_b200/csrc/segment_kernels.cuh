@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           mm[1] = 0ull;
         }
         ptx::named_bar(kBarEpi, kEpiThreads);
-        if (n > static_cast<uint32_t>(kTopK)) {
+        if (n > static_cast<uint32_t>(kCap - 4 * kTileKeys)) {  // fewer than two tile pairs of room
           group_minmax<kEpiThreads, kBarEpi>(cand, n, mm, et);
           uint32_t kept = 0;
           uint64_t T = group_cut<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, &kept);
@@ -558,6 +558,8 @@ static_assert(kTopK * 8 + 3 * 2048 * 4 + kTopK * 2 <= kMergeKeys * 8, "ordering 
 static_assert(2 * (kM_SmemBytes + 1024) <= 233472, "two merge CTAs per SM");
 
 struct MergeSelectLayout {
+  static constexpr bool kSolo = false;
+  static constexpr int kSoloTmp = 0, kSoloD = 0, kSoloCnt = 0;
   static constexpr int kCand = kM_OffCand, kHist = kM_OffHist, kTot = kM_OffTot, kMisc = kM_OffMisc;
   static constexpr int kFinal = kM_OffFinal, kRankTmp = kM_OffCand, kRankCnt = kM_OffCand + kTopK * 8;
   static constexpr int kRankD = kRankCnt + 3 * 2048 * 4;

@@ -310,10 +310,11 @@ __device__ __forceinline__ uint32_t half16(const uint32_t* a, uint32_t d) {
   return (a[d >> 1] >> ((d & 1u) * 16u)) & 0xFFFFu;
 }
 
-// Ranks the n <= 2048 unique keys of keys[] in descending order and hands
-// every key to the emitter with its rank: emit.load(key) fetches what is
-// written for the key (issued for all of a thread's keys before any store),
-// emit.store(rank, value) writes it, emit.pad(i) fills ranks n..2047.
+// Ranks the n <= 256 * KPT unique keys of keys[] in descending order and
+// hands each of the best 2048 to the emitter with its rank: emit.load(key)
+// fetches what is written for the key (issued for all of a thread's keys
+// before any store), emit.store(rank, value) writes it, emit.pad(i) fills
+// ranks n..2047 when n < 2048. tmp and tmpd hold 256 * KPT entries.
 // 256 threads (t = 0..255) synchronised by barrier BAR; kmin <= every key <=
 // kmax. Instead of a sorting network (which on 256 threads is bound by
 // shared-memory traffic or shuffle latency at tens of thousands of cycles for
@@ -331,7 +332,7 @@ __device__ __forceinline__ uint32_t half16(const uint32_t* a, uint32_t d) {
 // When the score range is empty or not finite the 12 key bits below the
 // common prefix of kmin and kmax are used instead (equal scores then spread
 // by position).
-template <int BAR, class Emit>
+template <int BAR, int KPT, class Emit>
 __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n, uint64_t kmin, uint64_t kmax,
                                                 const RankScratch sc, Emit& emit) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
@@ -361,17 +362,18 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
     }
     return static_cast<uint32_t>(k >> shift) & static_cast<uint32_t>(kRankBuckets - 1);
   };
-  uint64_t k[8];
-  uint32_t d[8];
+  static_assert(256 * KPT >= kTopK, "at least 2048 keys");
+  uint64_t k[KPT];
+  uint32_t d[KPT];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < KPT; ++j) {
     const uint32_t i = t + 256 * j;
     k[j] = i < n ? keys[i] : 0ull;
     d[j] = bucket(k[j]);
   }
   group_sync<256, BAR>();
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < KPT; ++j)
     if (t + 256 * j < n) atomicAdd(&sc.cnt[d[j] >> 1], 1u << ((d[j] & 1u) * 16u));
   group_sync<256, BAR>();
   // Exclusive scan in descending bucket order; thread t owns words
@@ -404,16 +406,16 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
   }
   group_sync<256, BAR>();
   {  // scatter: all slot atomics first, then the stores that need them
-    uint32_t slot[8];
+    uint32_t slot[KPT];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < KPT; ++j) {
       const uint32_t sh = (d[j] & 1u) * 16u;
       slot[j] = (t + 256 * j < n)
                     ? half16(sc.start, d[j]) + ((atomicAdd(&sc.fill[d[j] >> 1], 1u << sh) >> sh) & 0xFFFFu)
                     : 0u;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < KPT; ++j)
       if (t + 256 * j < n) {
         sc.tmp[slot[j]] = k[j];
         sc.tmpd[slot[j]] = static_cast<uint16_t>(d[j]);
@@ -423,9 +425,10 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
   // In-bucket ranks. First pass: the first four keys of every bucket, as
   // straight-line code over all of a thread's keys (their load chains
   // overlap); second pass: the rest of the rare buckets holding more.
-  uint32_t r[8], b0[8], c[8];
+  constexpr uint32_t kLast = 256u * KPT - 1u;
+  uint32_t r[KPT], b0[KPT], c[KPT];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
+  for (int j = 0; j < KPT; ++j) {
     const uint32_t i = t + 256 * j;
     const bool live = i < n;
     const uint32_t ii = live ? i : 0u;
@@ -439,20 +442,21 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       const uint32_t q = b0[j] + m;
-      rr += (static_cast<uint32_t>(m) < c[j] && sc.tmp[q < 2047u ? q : 2047u] > k[j]) ? 1u : 0u;
+      rr += (static_cast<uint32_t>(m) < c[j] && sc.tmp[q < kLast ? q : kLast] > k[j]) ? 1u : 0u;
     }
     r[j] = b0[j] + rr;
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+  for (int j = 0; j < KPT; ++j)
     for (uint32_t q = b0[j] + 4; q < b0[j] + c[j]; ++q) r[j] += (sc.tmp[q] > k[j]) ? 1u : 0u;
-  typename Emit::Value v[8];
+  // Only the best 2048 are written (n may exceed 2048 when KPT > 8).
+  typename Emit::Value v[KPT];
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (t + 256 * j < n) v[j] = emit.load(k[j]);
+  for (int j = 0; j < KPT; ++j)
+    if (t + 256 * j < n && r[j] < static_cast<uint32_t>(kTopK)) v[j] = emit.load(k[j]);
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    if (t + 256 * j < n) emit.store(r[j], v[j]);
+  for (int j = 0; j < KPT; ++j)
+    if (t + 256 * j < n && r[j] < static_cast<uint32_t>(kTopK)) emit.store(r[j], v[j]);
   for (uint32_t i = n + t; i < static_cast<uint32_t>(kTopK); i += 256) emit.pad(i);
 }
 
