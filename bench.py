@@ -48,6 +48,9 @@ def traffic_per_launch(config, kernel):
 DOMINANT = {"segmented": "dsa::segment_stream_kernel", "cluster": "dsa::indexer_kernel<0>",
             "cluster-split": "dsa::indexer_kernel<0>"}
 PREFILL_CONFIGS = (3, 4)
+# Configs whose single sequence is split along the key axis across ranks
+# (every rank holds the same inputs; partial top-K, NCCL all-gather, merge).
+KEY_SHARDED_CONFIGS = (4,)
 FLOP_PER_KEY = 64 * 128 * 2  # one query row against one key: 64 heads x 128-dim dot products
 
 
@@ -161,15 +164,38 @@ def main():
     pkg = importlib.import_module(PKG_NAME)
     pkg._lib.load()
 
-    w = wl.config(args.config, device=dev, seed=args.config + 1000 * rank, scale_batch=args.batch_scale)
+    key_sharded = world > 1 and args.config in KEY_SHARDED_CONFIGS
+    seed = args.config if key_sharded else args.config + 1000 * rank
+    w = wl.config(args.config, device=dev, seed=seed, scale_batch=args.batch_scale)
     B = w.batch
     out = torch.empty((B, 2048), dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
     stream = torch.cuda.current_stream(dev)
 
-    def call():
-        pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, out)
-        return pkg.last_launch_count()
+    if key_sharded:
+        sh = importlib.import_module(PKG_NAME + ".sharding")
+        counts = {}
+
+        def pfn(*a):
+            r = pkg.indexer_partial(*a)
+            counts["p"] = pkg.last_launch_count()
+            return r
+
+        def mfn(*a):
+            r = pkg.indexer_merge(*a)
+            counts["m"] = pkg.last_launch_count()
+            return r
+
+        def run_sharded(q, kc, wt, sl, bt):
+            out.copy_(sh.key_sharded_topk(q, kc, wt, sl, bt, partial_fn=pfn, merge_fn=mfn))
+            return counts["p"] + counts["m"]
+
+        def call():
+            return run_sharded(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
+    else:
+        def call():
+            pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, out)
+            return pkg.last_launch_count()
 
     def barrier():
         if world > 1:
@@ -188,11 +214,17 @@ def main():
 
     # The step is captured once into a CUDA graph, so the device-timed region
     # measures the kernels, not Python launch overhead (the e2e region below
-    # keeps direct calls).
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=cap_stream):
+    # keeps direct calls). Key-sharded steps (NCCL collectives, milliseconds
+    # long) are launched directly.
+    graph = None
+    if key_sharded:
         per_step = call()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap_stream):
+            per_step = call()
+        torch.cuda.synchronize()
 
     # ---------------- device-timed region ----------------
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -204,7 +236,10 @@ def main():
         for i in range(args.steps):
             flush.zero_()
             starts[i].record(stream)
-            graph.replay()
+            if graph is not None:
+                graph.replay()
+            else:
+                call()
             ends[i].record(stream)
             launches += per_step
         torch.cuda.synchronize()
@@ -243,7 +278,10 @@ def main():
         d_w.copy_(h_w, non_blocking=True)
         d_sl.copy_(h_sl, non_blocking=True)
         d_bt.copy_(h_bt, non_blocking=True)
-        pkg.launch_topk_c(d_q, w.k_cache, d_w, d_sl, d_bt, out)
+        if key_sharded:
+            run_sharded(d_q, w.k_cache, d_w, d_sl, d_bt)
+        else:
+            pkg.launch_topk_c(d_q, w.k_cache, d_w, d_sl, d_bt, out)
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -280,12 +318,13 @@ def main():
                          f"through the PyTorch CPU restatement (oracle/reference_torch.py), {dt:.2f} s"}
 
     if rank == 0:
-        kernel = DOMINANT.get(path, path)
+        kernel = "dsa::indexer_kernel<2> (partial, key range)" if key_sharded else DOMINANT.get(path, path)
         tr = traffic_per_launch(args.config, kernel)
         if args.config in PREFILL_CONFIGS:
             # K is L2-resident (one sequence): the contraction on the tensor
             # cores bounds the kernel. B200's dense fp8 rate is twice bf16.
-            flops = w.visible_keys() * FLOP_PER_KEY
+            # Key-sharded: each rank's partial kernel scores 1/world of the keys.
+            flops = w.visible_keys() * FLOP_PER_KEY // (world if key_sharded else 1)
             achieved = flops / (kms_max * 1e-3) / 1e12
             roof = {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16, "unit": "TFLOP/s",
                     "frac": achieved / (2 * bf16), "traffic": tr,
@@ -299,15 +338,21 @@ def main():
                      "kernel_timing": "CUDA events on the launching stream around the kernel, "
                                       "separate pass of the same steps"})
         line = {
-            "metric": METRIC, "value": B * world / (ms_max * 1e-3), "unit": "queries/s", "n_gpus": world,
+            "metric": METRIC, "value": B * (1 if key_sharded else world) / (ms_max * 1e-3), "unit": "queries/s",
+            "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
+            "scaling": "strong" if key_sharded else "weak", "vs_baseline": None,
+            "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": w.name + ("" if args.batch_scale == 1.0 else f" (batch x{args.batch_scale})"),
-                       "batch_per_gpu": B, "global_batch": B * world,
-                       "visible_keys_per_gpu": w.visible_keys(), "max_pages": w.max_pages,
-                       "pool_pages": w.num_pages, "parallelism": f"request-sharded x{world}",
+                       "batch_per_gpu": B, "global_batch": B if key_sharded else B * world,
+                       "visible_keys_per_gpu": w.visible_keys() // (world if key_sharded else 1),
+                       "max_pages": w.max_pages,
+                       "pool_pages": w.num_pages,
+                       "parallelism": f"key-sharded x{world} (NCCL all-gather + merge)" if key_sharded
+                       else f"request-sharded x{world}",
                        "l2": "flushed (256 MB write) before every timed step"},
-            "e2e": {"value": B * world / (e2e_max * 1e-3), "unit": "queries/s", "h2d_bytes_per_step": h2d,
+            "e2e": {"value": B * (1 if key_sharded else world) / (e2e_max * 1e-3), "unit": "queries/s",
+                    "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max,
                     "kcache": "resident in HBM (persistent serving state)"},
             "roofline": roof,
