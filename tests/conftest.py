@@ -47,6 +47,11 @@ def load_golden(name):
         kind = spec.pop("kind")
         if kind == "config":
             w = W.config(spec["idx"])
+        elif kind == "config_rows":
+            full = W.config(spec["idx"])
+            idx = torch.as_tensor(spec["rows"])
+            w = W.Workload(full.name, full.q[idx].contiguous(), full.k_cache, full.weights[idx].contiguous(),
+                           full.seq_lens[idx].contiguous(), full.block_table[idx].contiguous())
         elif kind == "custom":
             w = W.custom(spec.pop("seq_lens"), **spec)
         else:
