@@ -263,21 +263,32 @@ def main():
     kernel_ms = sum(kms) / len(kms)
 
     # ---------------- end-to-end region (host buffers) ----------------
-    h_q = w.q.view(torch.uint8).cpu().pin_memory()
-    h_w = w.weights.cpu().pin_memory()
-    h_sl = w.seq_lens.cpu().pin_memory()
-    h_bt = w.block_table.cpu().pin_memory()
+    # A serving loop stages the step's small inputs (q, weights, seq_lens,
+    # block table) in one pinned host buffer and moves them with one copy;
+    # the result comes back with another. Both copies are inside the timed
+    # region; the K cache is resident device state.
+    def align(n):
+        return (n + 255) // 256 * 256
+    parts = [w.q.view(torch.uint8).reshape(-1), w.weights.view(torch.uint8).reshape(-1),
+             w.seq_lens.view(torch.uint8).reshape(-1), w.block_table.view(torch.uint8).reshape(-1)]
+    offs, off = [], 0
+    for t in parts:
+        offs.append(off)
+        off = align(off + t.numel())
+    h_in = torch.empty(off, dtype=torch.uint8).pin_memory()
+    for t, o in zip(parts, offs):
+        h_in[o:o + t.numel()].copy_(t.cpu())
+    d_in = torch.empty(off, dtype=torch.uint8, device=dev)
+    d_q = d_in[offs[0]:offs[0] + parts[0].numel()].view(torch.float8_e4m3fn).view(w.q.shape)
+    d_w = d_in[offs[1]:offs[1] + parts[1].numel()].view(torch.float32).view(w.weights.shape)
+    d_sl = d_in[offs[2]:offs[2] + parts[2].numel()].view(torch.int32).view(w.seq_lens.shape)
+    d_bt = d_in[offs[3]:offs[3] + parts[3].numel()].view(torch.int32).view(w.block_table.shape)
     h_out = torch.empty((B, 2048), dtype=torch.int32).pin_memory()
-    d_q = torch.empty_like(w.q)
-    d_w, d_sl, d_bt = torch.empty_like(w.weights), torch.empty_like(w.seq_lens), torch.empty_like(w.block_table)
-    h2d = h_q.numel() + h_w.numel() * 4 + h_sl.numel() * 4 + h_bt.numel() * 4
+    h2d = sum(t.numel() for t in parts)
     d2h = h_out.numel() * 4
 
     def e2e_call():
-        d_q.view(torch.uint8).copy_(h_q, non_blocking=True)
-        d_w.copy_(h_w, non_blocking=True)
-        d_sl.copy_(h_sl, non_blocking=True)
-        d_bt.copy_(h_bt, non_blocking=True)
+        d_in.copy_(h_in, non_blocking=True)
         if key_sharded:
             run_sharded(d_q, w.k_cache, d_w, d_sl, d_bt)
         else:
