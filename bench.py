@@ -343,8 +343,13 @@ def main():
                     "algorithmic_flops_per_launch": flops}
         else:
             achieved = kbytes / (kms_max * 1e-3) / 1e9
+            # Beside the K-cache bytes (the roofline unit): every byte the call
+            # touches once (q, weights, seq_lens, block table, output).
+            total = (kbytes + w.q.numel() + w.weights.numel() * 4 + w.seq_lens.numel() * 4
+                     + w.block_table.numel() * 4 + B * 2048 * 4)
             roof = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                    "traffic": tr, "peak_source": peak_src, "algorithmic_bytes_per_launch": kbytes}
+                    "traffic": tr, "peak_source": peak_src, "algorithmic_bytes_per_launch": kbytes,
+                    "total_bytes_per_launch": total}
         roof.update({"kernel": kernel, "kernel_ms": kms_max, "schedule": path,
                      "kernel_timing": "CUDA events on the launching stream around the kernel, "
                                       "separate pass of the same steps"})
