@@ -370,14 +370,23 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     return cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
   };
   // More clusters than fit at once: serve the longest rows first so that no
-  // long row starts in the last wave.
+  // long row starts in the last wave. Small batches rank their rows inside
+  // the kernel (no plan launch); larger ones get a one-CTA plan kernel.
   if (prm.batch > 1 && static_cast<int64_t>(G) * prm.batch > 2 * num_sms) {
-    int32_t* order = static_cast<int32_t*>(workspace(stream, static_cast<size_t>(prm.batch) * sizeof(int32_t)));
-    if (order) {
-      lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order);
-      if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-      params.order = order;
-      launches = 2;
+    int32_t* order = nullptr;
+    if (prm.batch <= kInKernelOrderMax) {
+      params.order = nullptr;
+      params.order_base = 0;
+    } else {
+      order = static_cast<int32_t*>(workspace(stream, static_cast<size_t>(prm.batch) * sizeof(int32_t)));
+      if (order) {
+        lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order);
+        if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+        params.order = order;
+        launches = 2;
+      }
+    }
+    if (order || params.order_base >= 0) {
       // When the short rows fit at two CTAs each, run everything in one
       // wave: the R longest rows at G CTAs and the rest at 2, as two
       // launches on two streams (DSA_TOPK_SPLIT=0 turns this off).
@@ -392,13 +401,16 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
         if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
         IndexerParams lo = params;
-        lo.order = order + R;
+        if (order)
+          lo.order = order + R;
+        else
+          lo.order_base = static_cast<int32_t>(R);
         if ((rc = launch(params, R, G, stream)) != DSA_OK) return rc;
         if ((rc = launch(lo, prm.batch - R, kGLow, side)) != DSA_OK) return rc;
         if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
         timer.stop();
-        t_last_launches = 3;
+        t_last_launches = launches + 1;
         t_last_path = "cluster-split";
         return DSA_OK;
       }
@@ -460,7 +472,7 @@ int launch_segmented(const void* q, const void* kcache, const float* w, const In
   const size_t o_n = off;
   off = align256(off + 4 * slots);
   const size_t o_cand = off;
-  off = align256(off + static_cast<size_t>(8) * kCap * slots);
+  off = align256(off + static_cast<size_t>(8) * kSegCap * slots);
   uint8_t* ws = static_cast<uint8_t*>(workspace(stream, off));
   if (!ws) return DSA_OK;
   CUtensorMap tk, ts, tq, tw;

@@ -42,7 +42,8 @@ constexpr int kTileKeys = 128;
 constexpr int kStages = 4;
 constexpr int kThreads = 320;     // 10 warps
 constexpr int kEpiThreads = 256;  // warps 2..9
-constexpr int kCap = 3072;        // candidate keys per CTA
+constexpr int kCap = 4096;        // candidate keys per CTA
+constexpr int kSoloCap = 3072;    // candidates a one-CTA row ranks at once (12 per thread)
 constexpr int kTmemBufs = 4;
 constexpr int kTmemCols = kTmemBufs * kHeads;
 
@@ -70,24 +71,28 @@ constexpr int kOffRankTmp = kOffFinal + kTopK * 8;        // 2048 x 8
 constexpr int kOffRankCnt = kOffRankTmp + kTopK * 8;      // 3 x 2048 x 4 (cnt, start, fill)
 constexpr int kOffRankD = kOffRankCnt + 3 * 2048 * 4;     // 2048 x 2 (bucket of each tmp slot)
 static_assert(kOffRankD + kTopK * 2 <= kOffQ, "ordering scratch must fit in the K ring");
-// One-CTA rows rank all kCap candidates in place of the cluster select; the
-// K ring then holds that ordering's scratch instead.
-constexpr int kOffSoloTmp = kOffK;                        // kCap x 8
-constexpr int kOffSoloD = kOffSoloTmp + kCap * 8;         // kCap x 2
-constexpr int kOffSoloCnt = kOffSoloD + kCap * 2;         // 3 x 2048 x 4
+// One-CTA rows with up to kSoloCap candidates rank them all in place of the
+// cluster select; the K ring then holds that ordering's scratch instead.
+constexpr int kOffSoloTmp = kOffK;                        // kSoloCap x 8
+constexpr int kOffSoloD = kOffSoloTmp + kSoloCap * 8;     // kSoloCap x 2
+constexpr int kOffSoloCnt = kOffSoloD + kSoloCap * 2;     // 3 x 2048 x 4
 static_assert(kOffSoloCnt % 16 == 0 && kOffSoloCnt + 3 * 2048 * 4 <= kOffQ, "solo ordering scratch");
+static_assert(2 * (kSmemBytes + 1024) <= 233472, "two CTAs per SM");
 static_assert(kStages * 16384 % 1024 == 0, "K tiles must stay 1024-aligned");
 static_assert((2 * kStages + 2 * kTmemBufs + 1) * 8 <= 256, "barrier area");
 
 // Misc word indices (uint32 at kOffMisc).
 enum MiscWord : int {
   kMiscTmem = 0,   // TMEM base address
-  kMiscCount = 1,  // candidates in the buffer
+  kMiscCount = 1,  // candidates in the buffer (after a compaction)
   kMiscAbort = 2,  // pipeline abort flag
+  kMiscSlot = 3,   // epilogue: append counter in use at the end of the stream
   kMiscSel = 4,    // 3 words: digit scan result
   kMiscPub = 8,    // 2 words read by other CTAs of the cluster
   kMiscTotal = 10,
   kMiscOffset = 11,
+  kMiscRot = 12,    // 3 rotating append counters of the epilogue
+  kMiscNBase = 15,  // epilogue: candidates below the current append interval
   kMiscMM = 16,     // 2 x u64: min / max of the local candidates
   kMiscPubMM = 20,  // 2 x u64 read by other CTAs of the cluster
   kMiscWsum = 24,   // 8 words: scan scratch of the final ordering
@@ -107,7 +112,40 @@ struct IndexerParams {
   int64_t num_pages;
   int32_t max_pages;
   int32_t batch;
+  // >= 0: no order array; the cluster serves the row whose longest-first
+  // rank is order_base + cluster index, computed in the kernel (small
+  // batches: saves the plan launch).
+  int32_t order_base = -1;
 };
+
+constexpr int kInKernelOrderMax = 256;  // rows ranked in-kernel at most
+static_assert(kCap * 8 >= kInKernelOrderMax * 4, "in-kernel row ranking scratch (candidate buffer)");
+
+// Longest-first rank -> row, computed by every CTA from the clamped lengths
+// (ties: smaller row first, as the plan kernel's counting sort would give
+// within a bucket). All kThreads threads; `scratch` holds batch ints.
+__device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, int32_t* scratch,
+                                           uint32_t* result) {
+  const int64_t cap = static_cast<int64_t>(p.max_pages) * kPage;
+  for (int j = threadIdx.x; j < p.batch; j += kThreads) {
+    int64_t l = p.seq_lens[j];
+    l = l < 0 ? 0 : (l > cap ? cap : l);
+    scratch[j] = static_cast<int32_t>((l + 2 * kPage - 1) / (2 * kPage));  // tiles
+  }
+  if (threadIdx.x == 0) *result = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.batch; i += kThreads) {
+    const int32_t li = scratch[i];
+    int r = 0;
+    for (int j = 0; j < p.batch; ++j) {
+      const int32_t lj = scratch[j];
+      r += (lj > li || (lj == li && j < i)) ? 1 : 0;
+    }
+    if (r == target) *result = static_cast<uint32_t>(i);
+  }
+  __syncthreads();
+  return static_cast<int>(*result);
+}
 
 __device__ unsigned int g_dsa_status;
 
@@ -176,7 +214,7 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
   if constexpr (L::kSolo) {
-    if (G == 1 && n <= static_cast<uint32_t>(kCap)) {
+    if (G == 1 && n <= static_cast<uint32_t>(kSoloCap)) {
       // One CTA holds every candidate of the row: rank them all and emit the
       // best 2048 (no threshold search, exchange or second pass).
       if (tid == 0) {
@@ -196,10 +234,10 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
       const int64_t o = static_cast<int64_t>(b) * kTopK;
       if (kMode == kModeTopK) {
         EmitSlots e{p.out + o, bt_row};
-        block_rank_emit<kBarLow, kCap / 256>(cand, n, mm[0], mm[1], sc, e);
+        block_rank_emit<kBarLow, kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e);
       } else {
         EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
-        block_rank_emit<kBarLow, kCap / 256>(cand, n, mm[0], mm[1], sc, e);
+        block_rank_emit<kBarLow, kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e);
       }
       return;
     }
@@ -348,7 +386,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int lane = threadIdx.x & 31;
   const uint32_t G = ptx::cluster_nctarank();
   const uint32_t rank = ptx::cluster_ctarank();
-  const int b = p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G);
+  const int b = p.order_base >= 0
+                    ? row_of_rank(p, p.order_base + static_cast<int>(blockIdx.x / G),
+                                  reinterpret_cast<int32_t*>(smem + kOffCand), misc_nv + kMiscSel)
+                    : (p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G));
 
   // ---- request geometry (identical in every thread) ----
   int64_t len = p.seq_lens[b];
@@ -388,6 +429,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     ptx::fence_mbar_init();
     misc_nv[kMiscCount] = 0u;
     misc_nv[kMiscAbort] = 0u;
+    misc_nv[kMiscRot] = misc_nv[kMiscRot + 1] = misc_nv[kMiscRot + 2] = 0u;
+    misc_nv[kMiscNBase] = misc_nv[kMiscSlot] = 0u;
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_s);
     ptx::prefetch_tmap(&tm_q);
@@ -496,6 +539,21 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint64_t thr = 0;  // keys below thr can no longer reach the top 2048
     int since = 0;
     int check_every = kCap / (2 * kTileKeys);
+    // Candidates [0, n_base) were counted at the last check; the keys of the
+    // current interval take slots n_base + (rotating counter `slot`). Each
+    // warp stores a tile's keys one tile late, once its slot atomic has
+    // returned (pm/pkeep/pkey/pbase/pleader: the pending append).
+    uint32_t n_base = 0, slot = 0, pm = 0, pbase = 0;
+    int pleader = 0;
+    bool pkeep = false;
+    uint64_t pkey = 0;
+    auto flush = [&]() {
+      if (pm) {
+        const uint32_t pb = __shfl_sync(0xFFFFFFFFu, pbase, pleader);
+        if (pkeep) cand[n_base + pb + __popc(pm & lanemask_lt())] = pkey;
+      }
+      pm = 0u;
+    };
 #pragma unroll 1
     for (int i = grp; i < my_tiles; i += 2) {
       const int s = i % kStages;
@@ -553,46 +611,58 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
         const uint64_t key = pack_key(score, static_cast<uint32_t>(pos));
         const bool keep = valid && key >= thr;
+        flush();  // the previous tile's keys (their slot atomic has returned)
         const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+        pm = m;
+        pkeep = keep;
+        pkey = key;
         if (m) {
-          const int leader = __ffs(m) - 1;
-          uint32_t base = 0;
-          if (lane == leader) base = atomicAdd(misc_nv + kMiscCount, static_cast<uint32_t>(__popc(m)));
-          base = __shfl_sync(0xFFFFFFFFu, base, leader);
-          if (keep) cand[base + __popc(m & lanemask_lt())] = key;
+          pleader = __ffs(m) - 1;
+          pbase = 0u;
+          if (lane == pleader) pbase = atomicAdd(misc_nv + kMiscRot + slot, static_cast<uint32_t>(__popc(m)));
         }
         // After every check_every tile pairs the buffer may be nearly full:
-        // both groups meet and cut it back. The schedule depends only on tile
-        // counts, so all eight warps take the same barriers.
+        // both groups meet (one barrier), read the interval's count and move
+        // to the next counter; the one used two intervals ago, read by every
+        // warp before this barrier, is cleared for reuse. The schedule
+        // depends only on tile counts, so all eight warps take the same
+        // barriers.
         if (++since == check_every) {
           since = 0;
           if ((i >> 1) < n_pairs_full) {
+            flush();
             ptx::named_bar(kBarEpi, kEpiThreads);
-            uint32_t n = misc[kMiscCount];
-            if (et == 0) {
-              mm[0] = ~0ull;
-              mm[1] = 0ull;
-            }
-            ptx::named_bar(kBarEpi, kEpiThreads);
-            // Cut only when fewer than two tile pairs of room are left:
-            // between checks the threshold already rejects most keys, so
-            // the buffer fills slowly and most checks need no cut.
+            const uint32_t n = n_base + misc[kMiscRot + slot];
+            if (et == 0) misc_nv[kMiscRot + (slot + 2u) % 3u] = 0u;
+            n_base = n;
+            slot = (slot + 1u) % 3u;
+            // Cut only when fewer than two tile pairs of room are left, and
+            // then exactly to the best 2048: between checks the threshold
+            // rejects most keys, so cuts (and the checks, scheduled by the
+            // free room) stay rare.
             if (n > static_cast<uint32_t>(kCap - 4 * kTileKeys)) {
-              // Cheap safe cut; the exact selection only if the cut frees
-              // too little room. Keys below the cut can never reach the top
-              // 2048.
+              if (et == 0) {
+                mm[0] = ~0ull;
+                mm[1] = 0ull;
+              }
+              ptx::named_bar(kBarEpi, kEpiThreads);
               group_minmax<kEpiThreads, kBarEpi>(cand, n, mm, et);
-              uint32_t kept = 0;
-              uint64_t T = group_cut<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, &kept);
-              if (kept > static_cast<uint32_t>(kCap - 4 * kTileKeys))
-                T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
-              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, misc_nv + kMiscWsum, et);
+              const uint64_t T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
+              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount,
+                                                                     misc_nv + kMiscWsum, et);
               thr = T;
-              n = misc[kMiscCount];
+              n_base = misc[kMiscCount];
             }
-            check_every = static_cast<int>((kCap - n) / (2 * kTileKeys));
+            check_every = static_cast<int>((kCap - n_base) / (2 * kTileKeys));
           }
         }
+      }
+    }
+    if (kMode != kModeScores) {
+      flush();
+      if (et == 0) {  // uniform over the epilogue; read after the barrier below
+        misc_nv[kMiscNBase] = n_base;
+        misc_nv[kMiscSlot] = slot;
       }
     }
   }
@@ -622,7 +692,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
   if (kMode == kModeScores) return;
 
-  cluster_select_emit<kMode, StreamSelectLayout>(smem, base_addr, misc_nv[kMiscCount], G, rank, b, bt_row, p);
+  // Every epilogue warp stored its last keys before the barrier above.
+  const uint32_t n_final = misc_nv[kMiscNBase] + misc_nv[kMiscRot + misc_nv[kMiscSlot]];
+  cluster_select_emit<kMode, StreamSelectLayout>(smem, base_addr, n_final, G, rank, b, bt_row, p);
 }
 
 // Longest-first request order for the indexer's clusters (one CTA of 1024

@@ -10,7 +10,7 @@
 //                                    indexer_kernel (TMA ring -> tcgen05 MMA ->
 //                                    two epilogue groups) without draining
 //                                    between segments; at a segment's end its
-//                                    candidate keys (<= kCap) go to the
+//                                    candidate keys (<= kSegCap) go to the
 //                                    segment's workspace slot;
 //   segment_merge_kernel   (one cluster of G CTAs per row) reads the row's
 //                                    segment lists, filters them against a
@@ -26,6 +26,10 @@
 #include "indexer_kernel.cuh"
 
 namespace dsa {
+
+// Candidate keys per segment (the stream kernel's buffer and the length of a
+// workspace list); sized so the stream kernel keeps two CTAs per SM.
+constexpr int kSegCap = 3072;
 
 // ------------------------------------------------------------------ plan
 struct SegPlan {
@@ -155,8 +159,8 @@ constexpr int kS_OffQ = kS_OffK + kStages * 16384;           // 2 x 8192 (swizzl
 constexpr int kS_OffScale = kS_OffQ + 2 * 8192;              // kStages x 512
 constexpr int kS_OffW = kS_OffScale + kStages * 512;         // 2 x 256
 constexpr int kS_OffDesc = kS_OffW + 2 * 256;                // kStages x 32
-constexpr int kS_OffCand = kS_OffDesc + kStages * 32;        // kCap x 8
-constexpr int kS_OffHist = kS_OffCand + kCap * 8;            // 256 x 4
+constexpr int kS_OffCand = kS_OffDesc + kStages * 32;        // kSegCap x 8
+constexpr int kS_OffHist = kS_OffCand + kSegCap * 8;            // 256 x 4
 constexpr int kS_OffBar = kS_OffHist + 256 * 4;              // 20 x 8
 constexpr int kS_OffMisc = kS_OffBar + 256;                  // misc words
 constexpr int kS_SmemUsed = kS_OffMisc + 128;
@@ -168,7 +172,7 @@ struct StreamParams {
   const int32_t* block_table;
   const int4* segs;
   uint32_t* ctrl;
-  uint64_t* ws_cand;  // [slots][kCap]
+  uint64_t* ws_cand;  // [slots][kSegCap]
   uint32_t* ws_n;     // [slots]
   int64_t num_pages;
   int32_t max_pages;
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint64_t thr = 0;
     int since = 0;
-    int check_every = kCap / (2 * kTileKeys);
+    int check_every = kSegCap / (2 * kTileKeys);
     int lseg = 0;
 #pragma unroll 1
     for (int i = grp;; i += 2) {
@@ -467,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // segment's workspace slot and the buffer starts empty again.
         ptx::named_bar(kBarEpi, kEpiThreads);
         const uint32_t n = misc[kMiscCount];
-        uint64_t* dst = p.ws_cand + static_cast<size_t>(d.slot) * kCap;
+        uint64_t* dst = p.ws_cand + static_cast<size_t>(d.slot) * kSegCap;
         for (uint32_t j = et; j < n; j += kEpiThreads) dst[j] = cand[j];
         if (et == 0) {
           p.ws_n[d.slot] = n;
@@ -477,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (et == 0) ptx::mbar_arrive(bar_qempty + 8 * d.qb);  // weights of this segment no longer read
         thr = 0;
         since = 0;
-        check_every = kCap / (2 * kTileKeys);
+        check_every = kSegCap / (2 * kTileKeys);
         ++lseg;
       } else if (++since == check_every) {
         // Same cut schedule as indexer_kernel, within the segment.
@@ -489,17 +493,17 @@ __global__ void __launch_bounds__(kThreads, 2)
           mm[1] = 0ull;
         }
         ptx::named_bar(kBarEpi, kEpiThreads);
-        if (n > static_cast<uint32_t>(kCap - 4 * kTileKeys)) {  // fewer than two tile pairs of room
+        if (n > static_cast<uint32_t>(kSegCap - 4 * kTileKeys)) {  // fewer than two tile pairs of room
           group_minmax<kEpiThreads, kBarEpi>(cand, n, mm, et);
           uint32_t kept = 0;
           uint64_t T = group_cut<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, &kept);
-          if (kept > static_cast<uint32_t>(kCap - 4 * kTileKeys))
+          if (kept > static_cast<uint32_t>(kSegCap - 4 * kTileKeys))
             T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
-          group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, misc_nv + kMiscWsum, et);
+          group_compact<kEpiThreads, kBarEpi, kSegCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, misc_nv + kMiscWsum, et);
           thr = T;
           n = misc[kMiscCount];
         }
-        check_every = static_cast<int>((kCap - n) / (2 * kTileKeys));
+        check_every = static_cast<int>((kSegCap - n) / (2 * kTileKeys));
       }
     }
   }
@@ -553,7 +557,7 @@ constexpr int kM_OffSegOff = kM_OffSegN + kThreads * 4;       // kThreads x 4: l
 constexpr int kM_OffWsum = kM_OffSegOff + kThreads * 4;       // 16 x 4
 constexpr int kM_OffMisc = kM_OffWsum + 64;                   // misc words
 constexpr int kM_SmemBytes = kM_OffMisc + 128 + 1024;
-static_assert(kMergeKeys >= 2 * kCap + kTopK, "a cut buffer must take two more lists");
+static_assert(kMergeKeys >= 2 * kSegCap + kTopK, "a cut buffer must take two more lists");
 static_assert(kTopK * 8 + 3 * 2048 * 4 + kTopK * 2 <= kMergeKeys * 8, "ordering scratch must fit in the candidate buffer");
 static_assert(2 * (kM_SmemBytes + 1024) <= 233472, "two merge CTAs per SM");
 
@@ -630,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int k = 0; k < nfit; ++k) {
       const uint32_t mk = seg_n[k];
       const uint32_t dst = cand_addr + 8u * seg_off[k];
-      const uint64_t* src = mp.ws_cand + static_cast<size_t>(first + static_cast<int>(rank) + (c0 + k) * static_cast<int>(G)) * kCap;
+      const uint64_t* src = mp.ws_cand + static_cast<size_t>(first + static_cast<int>(rank) + (c0 + k) * static_cast<int>(G)) * kSegCap;
       for (uint32_t i = tid; i < mk; i += kThreads) ptx::cp_async8(dst + 8u * i, src + i);
       added += mk;
     }
@@ -638,7 +642,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncthreads();
     n += added;
     c0 += nfit;
-    if (c0 < mine && n > static_cast<uint32_t>(kMergeKeys - kCap)) {
+    if (c0 < mine && n > static_cast<uint32_t>(kMergeKeys - kSegCap)) {
       // The next list may not fit: keep the exact best 2048 (staged through
       // the survivor area, which no other CTA writes before the cluster
       // select below).
