@@ -143,6 +143,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch-scale", type=float, default=1.0,
                     help="profiling only: run the config with its batch scaled down (ncu captures)")
+    ap.add_argument("--op", choices=["indexer", "cache_write"], default="indexer",
+                    help="cache_write: the index-K cache writer (FP8 quantiser) instead of the indexer")
+    ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -155,6 +158,8 @@ def main():
 
     if args.impl == "reference":
         return reference_arm(args, rank, wl)
+    if args.op == "cache_write":
+        return cache_write_bench(args, rank, local)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -384,6 +389,54 @@ def main():
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def cache_write_bench(args, rank, local):
+    """The index-K cache writer: `--tokens` bf16 vectors of 128 values,
+    quantised into a paged FP8 cache at a random permutation of its slots
+    (every page gets all 64 of its tokens). HBM-bound: per token 256 B read,
+    8 B slot read, 132 B written. One process; rank 0 prints."""
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pkg = importlib.import_module(PKG_NAME)
+    T = args.tokens
+    pages = (T + 63) // 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    k = (torch.randn((T, 128), generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    slots = torch.randperm(pages * 64, generator=g, device=dev)[:T].to(torch.int64)
+    cache = torch.zeros((pages, 64, 1, 132), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        pkg.index_cache_write(k, slots, cache)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for a, b in ev:
+            flush.zero_()
+            a.record(st)
+            pkg.index_cache_write(k, slots, cache)
+            b.record(st)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    hbm, _, peak_src = peaks()
+    algo = T * (256 + 8 + 132)
+    achieved = algo / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "index-K cache writer tokens/s", "value": T / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> fp8_e4m3",
+            "data": "synthetic",
+            "config": {"workload": f"{T} tokens into {pages} pages, random slot permutation",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": algo, "kernel": "dsa::cache_write_kernel<true>"},
+            "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
 
 
 def reference_arm(args, rank, wl):

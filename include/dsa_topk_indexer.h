@@ -118,6 +118,24 @@ DSA_API int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cache, 
                                             int32_t* topk_indices, int64_t batch, int64_t max_pages,
                                             int64_t num_pages, void* stream);
 
+/* Index-K cache writer (the producer of the page format above; the
+ * reference only consumes it, solution/cuda/kernel.cu:22-25). Quantises
+ * `num_tokens` vectors of 128 values (`k`: bf16 or fp32, [num_tokens, 128],
+ * contiguous, 16-byte aligned, finite) to FP8 e4m3 with one fp32 scale per
+ * token: scale = max|x| / 448, inv = 448 / max|x| (both 1 when scale is not
+ * positive or inv not finite, e.g. an all-zero vector), values x * inv
+ * rounded to nearest even and saturated, and
+ * writes token t into slot `slots[t]` (int64 array, 16-byte aligned;
+ * page * 64 + offset) of `k_cache` ([num_pages, 8448] bytes): bytes
+ * [offset*128, +128) of the page and its fp32 scale at byte 8192 + offset*4.
+ * Negative slots are skipped; slots past num_pages*64 are skipped and flag
+ * DSA_STATUS_BAD_PAGE. Tokens sharing a slot: one of them wins.
+ * Asynchronous on `stream`. */
+#define DSA_DTYPE_BF16 0
+#define DSA_DTYPE_F32 1
+DSA_API int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* slots, void* k_cache,
+                                  int64_t num_tokens, int64_t num_pages, void* stream);
+
 /* Makes `device` the current CUDA device of the calling host thread for this
  * library (the entry points above run on the current device). Callers that
  * link their own CUDA runtime (PyTorch, TVM-FFI hosts) call it with the

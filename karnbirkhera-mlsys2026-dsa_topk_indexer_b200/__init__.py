@@ -159,6 +159,31 @@ def indexer_merge(cand_scores, cand_pos, seq_lens, block_table, topk_indices=Non
     return topk_indices
 
 
+def index_cache_write(k, slots, k_index_cache_fp8):
+    """Quantises index-K vectors into the paged FP8 cache the indexer reads
+    (in place): k [T, 128] bfloat16 or float32, slots [T] int64 (page * 64 +
+    offset; negative = skip), k_index_cache_fp8 [num_pages, 64, 1, 132]
+    (uint8 or float8 view), all on one CUDA device. Per token: scale =
+    max|x| / 448 (1 for an all-zero vector), bytes = e4m3(x * 448 / max|x|)."""
+    torch = _torch()
+    _require(k.dim() == 2 and k.shape[1] == 128 and k.is_contiguous(), "k must be contiguous [T, 128]")
+    _require(k.dtype in (torch.bfloat16, torch.float32), "k must be bfloat16 or float32")
+    _require(slots.dtype == torch.int64 and slots.dim() == 1 and slots.shape[0] == k.shape[0]
+             and slots.is_contiguous(), "slots must be contiguous int64 [T]")
+    _require(k_index_cache_fp8.is_contiguous() and k_index_cache_fp8.numel() * k_index_cache_fp8.element_size()
+             % 8448 == 0, "k_index_cache_fp8 must be contiguous pages of 8448 bytes")
+    dev = k.device
+    _require(slots.device == dev and k_index_cache_fp8.device == dev, "tensors must share one device")
+    num_pages = k_index_cache_fp8.numel() * k_index_cache_fp8.element_size() // 8448
+    lib = _lib.load()
+    _select(lib, dev)
+    with torch.cuda.device(dev):
+        rc = lib.dsa_index_cache_write(_ptr(k), 0 if k.dtype == torch.bfloat16 else 1, _ptr(slots),
+                                       _ptr(k_index_cache_fp8), k.shape[0], num_pages, _stream(dev))
+    _lib.check(rc, "index_cache_write")
+    return k_index_cache_fp8
+
+
 def device_status(device=0, clear=True):
     """Status bits the kernels raised on `device` since the last clear."""
     v = ctypes.c_uint32(0)

@@ -17,6 +17,7 @@
 #include "dsa_topk_indexer.h"
 #include "indexer_kernel.cuh"
 #include "segment_kernels.cuh"
+#include "cache_writer.cuh"
 
 namespace dsa {
 
@@ -184,7 +185,11 @@ int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
         return DSA_ERR_CUDA;
     }
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&merge_kernel),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmem) != cudaSuccess)
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&cache_write_kernel<true>),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<true>::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&cache_write_kernel<false>),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<false>::kSmem) != cudaSuccess)
       return DSA_ERR_CUDA;
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_stream_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kS_SmemBytes) != cudaSuccess ||
@@ -793,4 +798,32 @@ extern "C" int dsa_topk_indexer_kernel_ms(float* ms) {
   if (!ms || !t_timed) return DSA_ERR_INVALID_ARG;
   if (cudaEventSynchronize(t_ev_end) != cudaSuccess) return DSA_ERR_CUDA;
   return cudaEventElapsedTime(ms, t_ev_begin, t_ev_end) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+extern "C" int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* slots, void* k_cache,
+                                     int64_t num_tokens, int64_t num_pages, void* stream) {
+  t_last_launches = 0;
+  if (num_tokens < 0 || num_pages < 1) return DSA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return DSA_OK;
+  if (!k || !slots || !k_cache || (k_dtype != DSA_DTYPE_BF16 && k_dtype != DSA_DTYPE_F32))
+    return DSA_ERR_INVALID_ARG;
+  if (!aligned16(k) || !aligned16(k_cache) || !aligned16(slots)) return DSA_ERR_MISALIGNED;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  const bool bf16 = k_dtype == DSA_DTYPE_BF16;
+  const int64_t per_chunk = bf16 ? WriterGeom<true>::kTokens : WriterGeom<false>::kTokens;
+  int64_t blocks = (num_tokens + per_chunk - 1) / per_chunk;
+  const int64_t cap = static_cast<int64_t>(num_sms) * 4;  // four 50 KB rings per SM
+  if (blocks > cap) blocks = cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bf16)
+    cache_write_kernel<true><<<static_cast<unsigned>(blocks), 32 * kWriterWarps, WriterGeom<true>::kSmem, st>>>(
+        k, slots, static_cast<uint8_t*>(k_cache), num_tokens, num_pages);
+  else
+    cache_write_kernel<false><<<static_cast<unsigned>(blocks), 32 * kWriterWarps, WriterGeom<false>::kSmem, st>>>(
+        k, slots, static_cast<uint8_t*>(k_cache), num_tokens, num_pages);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 1;
+  return DSA_OK;
 }

@@ -291,6 +291,18 @@ __device__ __forceinline__ void cp_async8(uint32_t dst_smem, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Asynchronous 16-byte global -> shared copy (both 16-byte aligned), L2 only;
+// `src_bytes` < 16 zero-fills the rest (0: nothing is read).
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Programmatic dependent launch: grid_dep_wait blocks until the grid this one
 // depends on has completed and its memory is visible (returns at once when
 // the kernel was launched without that dependency); grid_dep_launch lets the

@@ -87,3 +87,32 @@ def indexer_shared_causal(q, k_cache, weights, seq_lens, block_table, chunk=256)
         for i in range(e - s):
             out[s + i] = topk_translate(final[i, :int(sl_all[s + i])], block_table[s + i])
     return out
+
+
+def cache_write(k, slots, k_cache):
+    """CPU restatement of the index-K cache writer (test infrastructure; the
+    reference has no writer and reads this format, solution/cuda/kernel.cu:
+    22-25). k [T, 128] bf16/fp32, slots [T] int64, k_cache [num_pages, ...]
+    uint8 with 8448 bytes per page, written in place. Per token: scale =
+    max|x| / 448 and inv = 448 / max|x| in fp32 (both 1 when scale is not
+    positive or inv not finite), bytes = e4m3(x * inv) with torch's
+    round-to-nearest-even cast (the products never exceed 448 by more than
+    the multiplication's rounding, which rounds back to 448)."""
+    flat = k_cache.view(-1, 8448)
+    x = k.to(torch.float32)
+    amax = x.abs().amax(dim=1)
+    c448 = torch.tensor(448.0, dtype=torch.float32)
+    scale = amax / c448
+    inv = c448 / amax
+    ok = (scale > 0) & torch.isfinite(inv)
+    scale = torch.where(ok, scale, torch.ones_like(scale))
+    inv = torch.where(ok, inv, torch.ones_like(inv))
+    q = (x * inv[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    for t in range(k.shape[0]):
+        s = int(slots[t])
+        if s < 0 or (s >> 6) >= flat.shape[0]:
+            continue
+        page, off = s >> 6, s & 63
+        flat[page, off * 128:(off + 1) * 128] = q[t]
+        flat[page, 8192 + off * 4:8192 + off * 4 + 4] = scale[t:t + 1].view(torch.uint8)
+    return k_cache
