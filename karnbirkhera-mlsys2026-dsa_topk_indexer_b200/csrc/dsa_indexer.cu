@@ -23,81 +23,75 @@ namespace dsa {
 
 // --------------------------------------------------------------- merge kernel
 // Merges nparts best-first candidate lists (score, logical position) of one
-// request into its final top-2048 physical slots. One 256-thread CTA per
-// request; candidates stream through a 4096-key shared buffer that is
-// compacted to the exact best 2048 after every part.
+// request into its final top-2048 physical slots (key-axis sharding: each
+// list is one key range's best 2048, already in descending key order). One
+// 256-thread CTA per request folds the lists in one at a time with a
+// merge-path merge that keeps the top 2048: thread t finds by binary search
+// how many of its 8 output ranks [8t, 8t+8) come from each list, then merges
+// those 8 sequentially. The result is sorted, so it is translated and written
+// directly. Missing entries (position < 0) become key 0, below every real key.
 constexpr int kMergeThreads = 256;
-constexpr int kMergeCap = 4096;
-// cand keys, histogram, misc words (count, digit scan, min/max, scan scratch),
-// then the ordering scratch (bucket counts, starts, fill, bucket of each slot).
-constexpr int kMergeSmem = kMergeCap * 8 + 256 * 4 + 128 + 3 * 2048 * 4 + kTopK * 2;
+constexpr int kMergeSmem = 3 * kTopK * 8;  // current result, next list, output
 
-__global__ void __launch_bounds__(kMergeThreads, 1)
+__device__ __forceinline__ void load_list(const float* __restrict__ sc, const int32_t* __restrict__ ps,
+                                          uint64_t* dst) {
+  for (int i = threadIdx.x; i < kTopK; i += kMergeThreads) {
+    const int32_t pos = ps[i];
+    dst[i] = pos >= 0 ? pack_key(sc[i], static_cast<uint32_t>(pos)) : 0ull;
+  }
+}
+
+// C[0..2048) = the 2048 largest of A[0..2048) and B[0..2048), descending
+// (both inputs descending; ties, only between padding zeros, go to B).
+__device__ __forceinline__ void merge_top(const uint64_t* A, const uint64_t* B, uint64_t* C) {
+  const int d = threadIdx.x * 8;
+  int lo = 0, hi = d;  // number of A elements among the first d outputs
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (A[mid] > B[d - 1 - mid]) lo = mid + 1; else hi = mid;
+  }
+  int i = lo, j = d - lo;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool take_a = i < kTopK && (j >= kTopK || A[i] > B[j]);
+    C[d + k] = take_a ? A[i] : B[j];
+    i += take_a ? 1 : 0;
+    j += take_a ? 0 : 1;
+  }
+}
+
+__global__ void __launch_bounds__(kMergeThreads)
     merge_kernel(const float* __restrict__ cand_scores, const int32_t* __restrict__ cand_pos, int nparts,
                  const int32_t* __restrict__ block_table, int32_t* __restrict__ out, int batch, int max_pages) {
   extern __shared__ __align__(16) uint8_t msmem[];
-  uint64_t* cand = reinterpret_cast<uint64_t*>(msmem);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(msmem + kMergeCap * 8);
-  uint32_t* misc = hist + 256;  // [0] count, [4..6] digit scan, [8..11] min/max, [16..23] scan scratch
-  unsigned long long* mm = reinterpret_cast<unsigned long long*>(misc + 8);
-  uint32_t* rank_cnt = misc + 32;
-  const int tid = threadIdx.x, lane = tid & 31;
+  uint64_t* cur = reinterpret_cast<uint64_t*>(msmem);
+  uint64_t* nxt = cur + kTopK;
+  uint64_t* res = nxt + kTopK;
   const int b = blockIdx.x;
-  if (tid == 0) misc[0] = 0u;
-  __syncthreads();
-  uint64_t thr = 0;
+  const int64_t row = static_cast<int64_t>(b) * kTopK;
+  const int64_t part = static_cast<int64_t>(batch) * kTopK;
+  load_list(cand_scores + row, cand_pos + row, cur);
 #pragma unroll 1
-  for (int j = 0; j < nparts; ++j) {
-    const int64_t row = (static_cast<int64_t>(j) * batch + b) * kTopK;
-#pragma unroll 1
-    for (int i0 = 0; i0 < kTopK; i0 += kMergeThreads) {
-      const int i = i0 + tid;
-      const int32_t pos = cand_pos[row + i];
-      const bool live = pos >= 0;
-      const uint64_t key = live ? pack_key(cand_scores[row + i], static_cast<uint32_t>(pos)) : 0ull;
-      const bool keep = live && key >= thr;
-      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
-      if (m) {
-        const int leader = __ffs(m) - 1;
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(misc, static_cast<uint32_t>(__popc(m)));
-        base = __shfl_sync(0xFFFFFFFFu, base, leader);
-        if (keep) cand[base + __popc(m & lanemask_lt())] = key;
-      }
-      // Lists are best-first: once a whole chunk is rejected, so is the rest.
-      if (!__syncthreads_or(keep)) break;
-    }
+  for (int j = 1; j < nparts; ++j) {
+    load_list(cand_scores + j * part + row, cand_pos + j * part + row, nxt);
     __syncthreads();
-    const uint32_t n = misc[0];
+    merge_top(cur, nxt, res);
     __syncthreads();
-    if (n > static_cast<uint32_t>(kTopK)) {
-      if (tid == 0) {
-        mm[0] = ~0ull;
-        mm[1] = 0ull;
-      }
-      __syncthreads();
-      group_minmax<kMergeThreads, 0>(cand, n, mm, tid);
-      thr = group_select<kMergeThreads, 0>(cand, n, kTopK, mm, hist, misc + 4, tid);
-      group_compact<kMergeThreads, 0, kMergeCap / kMergeThreads>(cand, n, thr, misc, misc + 16, tid);
-    }
+    uint64_t* t = cur;
+    cur = res;
+    res = t;
   }
   __syncthreads();
-  const uint32_t nsel = misc[0] < static_cast<uint32_t>(kTopK) ? misc[0] : static_cast<uint32_t>(kTopK);
-  if (tid == 0) {
-    mm[0] = ~0ull;
-    mm[1] = 0ull;
+  const int32_t* bt_row = block_table + static_cast<int64_t>(b) * max_pages;
+  int32_t v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint64_t key = cur[threadIdx.x * 8 + k];
+    const uint32_t pos = key_pos(key);
+    v[k] = key ? bt_row[pos >> 6] * kPage + static_cast<int32_t>(pos & 63u) : -1;
   }
-  __syncthreads();
-  group_minmax<kMergeThreads, 0>(cand, nsel, mm, tid);
-  RankScratch sc;
-  sc.tmp = cand + kTopK;
-  sc.cnt = rank_cnt;
-  sc.start = rank_cnt + 2048;
-  sc.fill = rank_cnt + 4096;
-  sc.tmpd = reinterpret_cast<uint16_t*>(rank_cnt + 6144);
-  sc.wsum = misc + 16;
-  EmitSlots e{out + static_cast<int64_t>(b) * kTopK, block_table + static_cast<int64_t>(b) * max_pages};
-  block_rank_emit<0, 8>(cand, nsel, mm[0], mm[1], sc, e);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) out[row + threadIdx.x * 8 + k] = v[k];
 }
 
 // Fills a float buffer (used for the -inf background of the score rows).
