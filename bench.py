@@ -146,6 +146,8 @@ def main():
     ap.add_argument("--op", choices=["indexer", "cache_write"], default="indexer",
                     help="cache_write: the index-K cache writer (FP8 quantiser) instead of the indexer")
     ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
+    ap.add_argument("--exchange", choices=["alltoall", "allgather"], default="alltoall",
+                    help="key-sharded configs at N>1: how the per-rank candidate lists meet")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -192,7 +194,7 @@ def main():
             return r
 
         def run_sharded(q, kc, wt, sl, bt):
-            out.copy_(sh.key_sharded_topk(q, kc, wt, sl, bt, partial_fn=pfn, merge_fn=mfn))
+            out.copy_(sh.key_sharded_topk(q, kc, wt, sl, bt, partial_fn=pfn, merge_fn=mfn, exchange=args.exchange))
             return counts["p"] + counts["m"]
 
         def call():
@@ -369,7 +371,10 @@ def main():
                        "visible_keys_per_gpu": w.visible_keys() // (world if key_sharded else 1),
                        "max_pages": w.max_pages,
                        "pool_pages": w.num_pages,
-                       "parallelism": f"key-sharded x{world} (NCCL all-gather + merge)" if key_sharded
+                       "parallelism": (f"key-sharded x{world} (NCCL all-to-all of candidate lists, merge, all-gather "
+                                       "of results)" if args.exchange == "alltoall" else
+                                       f"key-sharded x{world} (NCCL all-gather of candidate lists + merge)")
+                       if key_sharded
                        else f"request-sharded x{world}",
                        "l2": "flushed (256 MB write) before every timed step"},
             "e2e": {"value": B * (1 if key_sharded else world) / (e2e_max * 1e-3), "unit": "queries/s",

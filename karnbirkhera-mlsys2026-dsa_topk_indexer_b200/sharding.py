@@ -48,10 +48,18 @@ def _default_merge(cs, cp, sl, bt):
     return pkg.indexer_merge(cs, cp, sl, bt)
 
 
-def key_sharded_topk(q, kc, w, seq_lens, block_table, group=None, partial_fn=None, merge_fn=None, max_len=None):
+def key_sharded_topk(q, kc, w, seq_lens, block_table, group=None, partial_fn=None, merge_fn=None, max_len=None,
+                     exchange="alltoall"):
     """Top-2048 physical slots of every row, the key axis split over the ranks
     of `group`. Every rank holds the full inputs (the K cache pages of its
-    range must be resident) and returns the same full result."""
+    range must be resident) and returns the same full result.
+
+    exchange="allgather": every rank gathers every rank's [B, 2048]
+    candidate lists and merges all B rows. exchange="alltoall": rank r
+    receives only the lists of its B/world rows (all-to-all), merges those,
+    and the [B, 2048] int32 results are all-gathered: (world-1)/world of one
+    rank's lists cross the links instead of world-1 times all of them, and
+    the merge work is split world ways."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -62,8 +70,29 @@ def key_sharded_topk(q, kc, w, seq_lens, block_table, group=None, partial_fn=Non
     merge_fn = merge_fn or _default_merge
     cs, cp = partial_fn(q, kc, w, seq_lens, block_table, lo, hi)
     B = cs.shape[0]
-    cs_all = torch.empty((world * B, TOPK), dtype=cs.dtype, device=cs.device)
-    cp_all = torch.empty((world * B, TOPK), dtype=cp.dtype, device=cp.device)
-    dist.all_gather_into_tensor(cs_all, cs.contiguous(), group=group)
-    dist.all_gather_into_tensor(cp_all, cp.contiguous(), group=group)
-    return merge_fn(cs_all.view(world, B, TOPK), cp_all.view(world, B, TOPK), seq_lens, block_table)
+    if exchange == "allgather":
+        cs_all = torch.empty((world * B, TOPK), dtype=cs.dtype, device=cs.device)
+        cp_all = torch.empty((world * B, TOPK), dtype=cp.dtype, device=cp.device)
+        dist.all_gather_into_tensor(cs_all, cs.contiguous(), group=group)
+        dist.all_gather_into_tensor(cp_all, cp.contiguous(), group=group)
+        return merge_fn(cs_all.view(world, B, TOPK), cp_all.view(world, B, TOPK), seq_lens, block_table)
+    if exchange != "alltoall":
+        raise ValueError(f"exchange must be 'allgather' or 'alltoall', not {exchange!r}")
+    # Rows [bounds[r], bounds[r+1]) are merged on rank r.
+    bounds = [B * r // world for r in range(world + 1)]
+    sizes = [bounds[r + 1] - bounds[r] for r in range(world)]
+    mine = sizes[rank]
+    cs_in = torch.empty((world * mine, TOPK), dtype=cs.dtype, device=cs.device)
+    cp_in = torch.empty((world * mine, TOPK), dtype=cp.dtype, device=cp.device)
+    dist.all_to_all_single(cs_in, cs.contiguous(), [mine] * world, sizes, group=group)
+    dist.all_to_all_single(cp_in, cp.contiguous(), [mine] * world, sizes, group=group)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    per = (B + world - 1) // world  # equal all-gather blocks; short blocks padded
+    part = torch.full((per, TOPK), -1, dtype=torch.int32, device=cs.device)
+    if mine > 0:
+        part[:mine] = merge_fn(cs_in.view(world, mine, TOPK), cp_in.view(world, mine, TOPK),
+                               seq_lens[r0:r1].contiguous(), block_table[r0:r1].contiguous())
+    gathered = torch.empty((world * per, TOPK), dtype=torch.int32, device=cs.device)
+    dist.all_gather_into_tensor(gathered, part, group=group)
+    g = gathered.view(world, per, TOPK)
+    return torch.cat([g[r, :sizes[r]] for r in range(world)], dim=0)

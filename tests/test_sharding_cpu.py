@@ -61,26 +61,30 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, result_q):
+SHARD_LENS = [5000, 2100, 700, 0, 3333]  # 5 rows: the all-to-all blocks are uneven
+
+
+def _worker(rank, world, port, result_q, exchange):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         W = workloads()
         sh = __import__("importlib").import_module(package().__name__ + ".sharding")
-        w = W.custom([5000, 2100, 700, 0], seed=31)
+        w = W.custom(SHARD_LENS, seed=31)
         got = sh.key_sharded_topk(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table,
-                                  partial_fn=oracle_partial, merge_fn=oracle_merge)
+                                  partial_fn=oracle_partial, merge_fn=oracle_merge, exchange=exchange)
         result_q.put((rank, got.numpy()))
     finally:
         dist.destroy_process_group()
 
 
-def test_key_sharded_merge_equals_one_shot():
+@pytest.mark.parametrize("exchange", ["allgather", "alltoall"])
+def test_key_sharded_merge_equals_one_shot(exchange):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=120) for _ in range(world))
@@ -88,7 +92,7 @@ def test_key_sharded_merge_equals_one_shot():
         p.join(timeout=60)
         assert p.exitcode == 0
     W = workloads()
-    w = W.custom([5000, 2100, 700, 0], seed=31)
+    w = W.custom(SHARD_LENS, seed=31)
     ref = oracle.indexer(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
     for r in range(world):
         assert np.array_equal(results[r], ref)
