@@ -161,3 +161,42 @@ def custom(seq_lens, pool_pages=None, seed=0, device="cpu", max_pages=None, scal
     need = sum((int(s) + PAGE - 1) // PAGE for s in seq_lens)
     pool = pool_pages if pool_pages is not None else max(1, need + 3)
     return make_paged("custom", seq_lens, pool, seed, device, scale_dist, max_pages=max_pages)
+
+
+def load_safetensors_workload(path, seed=0, num_pages=None, k_init="normal", device="cpu"):
+    """One FlashInfer-Bench workload file: a safetensors file holding the
+    structural tensors `block_table` [B, max_num_pages] and `seq_lens` [B]
+    (int32), as the contest dataset stores them (the reference reads them
+    the same way, methodology/diagnostic_tests/run_ncu_profile.py:103-122).
+    q, weights and the K pages are synthesised from `seed`:
+      k_init="normal"  the benchmark distributions of this module (e4m3 of
+                       N(0,1) data, scales U[0.01, 0.1]) on every page;
+      k_init="randint" every cache byte uniform in [-128, 128), as the
+                       contest harness fills it (scale bytes included, so
+                       scales are arbitrary bit patterns and e4m3 NaN bytes
+                       occur: outputs then depend on NaN handling).
+    num_pages defaults to max(block_table) + 1."""
+    from safetensors.torch import load_file
+    t = load_file(path)
+    if "block_table" not in t or "seq_lens" not in t:
+        raise ValueError(f"{path}: expected tensors block_table and seq_lens, found {sorted(t)}")
+    bt = t["block_table"].to(torch.int32).contiguous()
+    sl = t["seq_lens"].to(torch.int32).reshape(-1).contiguous()
+    if bt.dim() != 2 or bt.shape[0] != sl.shape[0]:
+        raise ValueError(f"{path}: block_table {tuple(bt.shape)} does not match seq_lens {tuple(sl.shape)}")
+    n = int(bt.max()) + 1 if num_pages is None else int(num_pages)
+    if int(bt.min()) < 0 or int(bt.max()) >= n:
+        raise ValueError(f"{path}: block_table ids outside [0, {n})")
+    gen = _gen(seed, device)
+    if k_init == "normal":
+        k_cache = torch.zeros((n, PAGE, 1, DIM + 4), dtype=torch.uint8, device=device)
+        write_pages(k_cache, torch.arange(n), gen)
+    elif k_init == "randint":
+        k_cache = torch.randint(-128, 128, (n, PAGE, 1, DIM + 4), generator=gen, device=device,
+                                dtype=torch.int16).to(torch.int8).view(torch.uint8)
+    else:
+        raise ValueError(f"k_init must be 'normal' or 'randint', not {k_init!r}")
+    q, w = _queries(bt.shape[0], gen, device)
+    import os
+    return Workload(os.path.splitext(os.path.basename(path))[0], q, k_cache, w, sl.to(device), bt.to(device),
+                    {"pool_pages": n, "source": path, "k_init": k_init})
