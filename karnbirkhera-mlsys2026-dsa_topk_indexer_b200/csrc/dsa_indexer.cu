@@ -713,12 +713,16 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
   const int G = choose_cluster(batch, max_pages, num_sms);
   int launches = 1;
   if (batch > 1 && static_cast<int64_t>(G) * batch > 2 * num_sms) {
-    // The plan kernel writes all `batch` entries the indexer reads.
-    lpt_order_kernel<<<1, kPlanThreads, 0, st>>>(seq_lens, static_cast<int>(batch), static_cast<int>(max_pages),
-                                                 order);
-    if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-    p.order = order;
-    launches = 2;
+    if (batch <= kInKernelOrderMax) {
+      p.order_base = 0;  // rows ranked inside the kernel: no scratch at all
+    } else {
+      // The plan kernel writes all `batch` entries the indexer reads.
+      lpt_order_kernel<<<1, kPlanThreads, 0, st>>>(seq_lens, static_cast<int>(batch), static_cast<int>(max_pages),
+                                                   order);
+      if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+      p.order = order;
+      launches = 2;
+    }
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(G * batch), 1, 1);

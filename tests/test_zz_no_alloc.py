@@ -1,10 +1,11 @@
 """GPU: the no-allocation entry point, for callers that cannot allocate device
 memory (code running inside an allocator or memory-pool callback, or a server
-that has reserved all of HBM up front). It keeps its only scratch, the
-longest-first row order, in a fixed array inside the library instead of a
-per-stream workspace, so its results must equal those of the regular entry
-point. Two calls in a row with different inputs check that whatever the
-shared array holds from the previous call does not leak into the next one.
+that has reserved all of HBM up front). Batches up to 256 rows rank their rows
+inside the kernel; larger ones keep the longest-first row order in a fixed
+array inside the library instead of a per-stream workspace. Its results must
+equal those of the regular entry point. Consecutive calls with different
+inputs (two of them above 256 rows) check that whatever the shared array holds
+from the previous call does not leak into the next one.
 
 Kept in its own file, collected last, so a run that stops at the first
 failure has already run every other test.
@@ -42,7 +43,8 @@ def test_noalloc_matches_regular_entry_two_calls():
     # First input: 64 rows up to 32k keys -> more clusters than one wave, so
     # the row order is planned into the scratch array. Second input: other
     # rows and lengths, reusing the same array.
-    cases = [W.config(1, seed=41), W.custom([9000, 40, 0, 131072, 2049, 777] * 20, seed=42)]
+    cases = [W.config(1, seed=41), W.custom([9000, 40, 0, 131072, 2049, 777] * 20, seed=42),
+             W.custom([5000, 100, 2049, 0, 700] * 60, seed=43), W.custom([300, 4100, 64] * 100, seed=44)]
     for w_cpu in cases:
         w = w_cpu.to("cuda")
         ref = torch.full((w.batch, 2048), -7, dtype=torch.int32, device="cuda")
