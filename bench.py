@@ -13,6 +13,7 @@ its own batch (request sharding, no collective): weak scaling.
 import argparse
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -143,8 +144,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch-scale", type=float, default=1.0,
                     help="profiling only: run the config with its batch scaled down (ncu captures)")
-    ap.add_argument("--op", choices=["indexer", "cache_write"], default="indexer",
-                    help="cache_write: the index-K cache writer (FP8 quantiser) instead of the indexer")
+    ap.add_argument("--op", choices=["indexer", "cache_write", "sparse_attention"], default="indexer",
+                    help="cache_write: the index-K cache writer (FP8 quantiser); sparse_attention: the "
+                         "consumer of topk_indices (sparse MLA attention over the selected slots)")
+    ap.add_argument("--attn-tokens", type=int, default=128, help="sparse_attention: query tokens per step")
     ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
     ap.add_argument("--exchange", choices=["alltoall", "allgather"], default="alltoall",
                     help="key-sharded configs at N>1: how the per-rank candidate lists meet")
@@ -162,6 +165,8 @@ def main():
         return reference_arm(args, rank, wl)
     if args.op == "cache_write":
         return cache_write_bench(args, rank, local)
+    if args.op == "sparse_attention":
+        return sparse_attention_bench(args, rank, local)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -442,6 +447,97 @@ def cache_write_bench(args, rank, local):
                          "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "kernel": "dsa::cache_write_kernel<true>"},
             "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+
+
+def sparse_attention_bench(args, rank, local):
+    """Sparse MLA attention over 2048 selected slots per token (the consumer
+    of topk_indices): `--attn-tokens` tokens, 16 heads, a 1.2 GB pool of
+    bf16 latent (512) + rope (64) rows, slots drawn uniformly from the pool
+    (no reuse between tokens: the worst case for L2). HBM-bound gather:
+    per token 2048 x 1152 B of rows + 18 KB q + 16 KB out + 8 KB indices.
+    `value` is device-timed with inputs resident; `e2e` copies q and indices
+    from pinned host memory and the output and lse back every step."""
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pkg = importlib.import_module(PKG_NAME)
+    T, L, pages = args.attn_tokens, 2048, 16384
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    q_nope = torch.randn((T, 16, 512), generator=g, device=dev).to(torch.bfloat16)
+    q_pe = torch.randn((T, 16, 64), generator=g, device=dev).to(torch.bfloat16)
+    ckv = torch.randn((pages, 64, 512), generator=g, device=dev).to(torch.bfloat16)
+    kpe = torch.randn((pages, 64, 64), generator=g, device=dev).to(torch.bfloat16)
+    idx = torch.randint(0, pages * 64, (T, L), generator=g, device=dev, dtype=torch.int32)
+    out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
+    scale = 1.0 / math.sqrt(192.0)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+    # Warm-up on the capture stream (the library allocates its split buffers
+    # for that stream outside capture), then one CUDA graph of the call, so
+    # the device-timed region holds the kernel and not Python launch overhead.
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(st)
+    with torch.cuda.stream(cap):
+        for _ in range(max(3, args.warmup)):
+            flush.zero_()
+            pkg.sparse_attention(q_nope, q_pe, ckv, kpe, idx, scale, out, lse)
+    torch.cuda.synchronize()
+    launches = pkg.last_launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        pkg.sparse_attention(q_nope, q_pe, ckv, kpe, idx, scale, out, lse)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for a, b in ev:
+            flush.zero_()
+            a.record(st)
+            graph.replay()
+            b.record(st)
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    del graph
+    # End to end: inputs from pinned host memory, results back to it.
+    h_qn, h_qp, h_idx = q_nope.cpu().pin_memory(), q_pe.cpu().pin_memory(), idx.cpu().pin_memory()
+    h_out, h_lse = torch.empty_like(out, device="cpu").pin_memory(), torch.empty_like(lse, device="cpu").pin_memory()
+    d_qn, d_qp, d_idx = torch.empty_like(q_nope), torch.empty_like(q_pe), torch.empty_like(idx)
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps + 3):
+        flush.zero_()
+        a, b = ev2[i - 3] if i >= 3 else (None, None)
+        if a is not None:
+            a.record(st)
+        d_qn.copy_(h_qn, non_blocking=True)
+        d_qp.copy_(h_qp, non_blocking=True)
+        d_idx.copy_(h_idx, non_blocking=True)
+        pkg.sparse_attention(d_qn, d_qp, ckv, kpe, d_idx, scale, out, lse)
+        h_out.copy_(out, non_blocking=True)
+        h_lse.copy_(lse, non_blocking=True)
+        if b is not None:
+            b.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = sum(a.elapsed_time(b) for a, b in ev2) / args.steps
+    h2d = h_qn.numel() * 2 + h_qp.numel() * 2 + h_idx.numel() * 4
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+    hbm, _, peak_src = peaks()
+    algo = T * (L * 1152 + 16 * 576 * 2 + 16 * 512 * 2 + 16 * 4 + L * 4)
+    achieved = algo / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "sparse attention tokens/s (2048 slots each)", "value": T / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
+            "data": "synthetic",
+            "config": {"workload": f"{T} tokens x 2048 slots, 16 heads, ckv 512 + kpe 64, pool {pages} pages",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": algo, "kernel": "dsa::sparse_attention_kernel"},
+            "gpu_launches": args.steps * launches, "clocks": clk.summary()}), flush=True)
 
 
 def reference_arm(args, rank, wl):

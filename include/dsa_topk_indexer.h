@@ -136,6 +136,28 @@ DSA_API int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cache, 
 DSA_API int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* slots, void* k_cache,
                                   int64_t num_tokens, int64_t num_pages, void* stream);
 
+/* Sparse MLA attention over the selected slots: the consumer of
+ * topk_indices, operator dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64
+ * (named by the reference at FAQ.md:83 and EVALUATION.md:54-57,87; it
+ * carries no implementation). Per token t and head h (16 heads), over the
+ * entries s of sparse_indices[t] that are >= 0:
+ *   logit_s  = (q_nope[t,h] . ckv[s] + q_pe[t,h] . kpe[s]) * sm_scale
+ *   output[t,h] = sum_s softmax(logit)_s * ckv[s]       bf16 [T, 16, 512]
+ *   lse[t,h]    = log2(sum_s exp(logit_s))               fp32 [T, 16]
+ * Inputs (bf16, contiguous, 16-byte aligned): q_nope [T, 16, 512], q_pe
+ * [T, 16, 64], ckv_cache [num_pages, 64, 512], kpe_cache [num_pages, 64, 64];
+ * sparse_indices [T, num_indices] int32 slots page*64+offset (-1 = none;
+ * entries past num_pages*64 are ignored and flag DSA_STATUS_BAD_PAGE). A
+ * token with no valid entry gets output 0 and lse -inf. num_indices is at
+ * most 65536 (the operator uses 2048). Long lists are split across CTAs and
+ * combined on the device; the split buffers are library-owned and allocated
+ * (outside stream capture) the first time a shape needs them. Asynchronous
+ * on `stream`. */
+DSA_API int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe, const void* ckv_cache,
+                                        const void* kpe_cache, const int32_t* sparse_indices, float sm_scale,
+                                        void* output, float* lse, int64_t num_tokens, int64_t num_indices,
+                                        int64_t num_pages, void* stream);
+
 /* Makes `device` the current CUDA device of the calling host thread for this
  * library (the entry points above run on the current device). Callers that
  * link their own CUDA runtime (PyTorch, TVM-FFI hosts) call it with the

@@ -22,7 +22,7 @@ PAGE_SIZE = 64
 PAGE_BYTES = 8448
 TOPK = 2048
 
-__all__ = ["launch_topk_c", "indexer_scores", "indexer_partial", "indexer_merge", "device_status",
+__all__ = ["launch_topk_c", "indexer_scores", "indexer_partial", "indexer_merge", "sparse_attention", "device_status",
            "last_launch_count", "HEADS", "HEAD_DIM", "PAGE_SIZE", "PAGE_BYTES", "TOPK"]
 
 
@@ -182,6 +182,49 @@ def index_cache_write(k, slots, k_index_cache_fp8):
                                        _ptr(k_index_cache_fp8), k.shape[0], num_pages, _stream(dev))
     _lib.check(rc, "index_cache_write")
     return k_index_cache_fp8
+
+
+def sparse_attention(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, output=None, lse=None):
+    """Sparse MLA attention over the slots the indexer selected (the consumer
+    of ``topk_indices``, operator dsa_sparse_attention_h16_ckv512_kpe64_
+    topk2048_ps64). q_nope [T,16,512], q_pe [T,16,64], ckv_cache
+    [pages,64,512], kpe_cache [pages,64,64] bfloat16; sparse_indices [T, L]
+    int32 slots (-1 = none); sm_scale a float. Writes (and returns)
+    output [T,16,512] bfloat16 and lse [T,16] float32 (log2 of the softmax
+    denominator; -inf and a zero row when a token has no valid slot)."""
+    torch = _torch()
+    dev = q_nope.device
+    _require(dev.type == "cuda", "q_nope must be a CUDA tensor")
+    for name, t, shape in (("q_nope", q_nope, (16, 512)), ("q_pe", q_pe, (16, 64))):
+        _require(t.dtype == torch.bfloat16 and t.dim() == 3 and tuple(t.shape[1:]) == shape,
+                 f"{name} must be bfloat16 [T, {shape[0]}, {shape[1]}]")
+    T = q_nope.shape[0]
+    _require(q_pe.shape[0] == T, "q_pe must have as many tokens as q_nope")
+    for name, t, d in (("ckv_cache", ckv_cache, 512), ("kpe_cache", kpe_cache, 64)):
+        _require(t.dtype == torch.bfloat16 and t.dim() == 3 and t.shape[1] == 64 and t.shape[2] == d,
+                 f"{name} must be bfloat16 [num_pages, 64, {d}]")
+    _require(ckv_cache.shape[0] == kpe_cache.shape[0], "ckv_cache and kpe_cache must have the same pages")
+    _require(sparse_indices.dtype == torch.int32 and sparse_indices.dim() == 2 and sparse_indices.shape[0] == T,
+             "sparse_indices must be int32 [T, L]")
+    if output is None:
+        output = torch.empty(T, 16, 512, dtype=torch.bfloat16, device=dev)
+    if lse is None:
+        lse = torch.empty(T, 16, dtype=torch.float32, device=dev)
+    _require(output.dtype == torch.bfloat16 and tuple(output.shape) == (T, 16, 512), "output must be bf16 [T,16,512]")
+    _require(lse.dtype == torch.float32 and tuple(lse.shape) == (T, 16), "lse must be float32 [T,16]")
+    for name, t in (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache), ("kpe_cache", kpe_cache),
+                    ("sparse_indices", sparse_indices), ("output", output), ("lse", lse)):
+        _require(t.device == dev, f"{name} must be on {dev}")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    lib = _lib.load()
+    _select(lib, dev)
+    with torch.cuda.device(dev):
+        rc = lib.dsa_sparse_attention_launch(_ptr(q_nope), _ptr(q_pe), _ptr(ckv_cache), _ptr(kpe_cache),
+                                             _ptr(sparse_indices), ctypes.c_float(float(sm_scale)), _ptr(output),
+                                             _ptr(lse), T, sparse_indices.shape[1], ckv_cache.shape[0],
+                                             _stream(dev))
+    _lib.check(rc, "sparse_attention")
+    return output, lse
 
 
 def device_status(device=0, clear=True):

@@ -31,6 +31,7 @@ SIGNATURES = [
     ("dsa_topk_indexer_last_launch_count", _I32, []),
     ("dsa_topk_indexer_last_path", ctypes.c_char_p, []),
     ("dsa_index_cache_write", _I32, [_P, _I32, _P, _P, _I64, _I64, _P]),
+    ("dsa_sparse_attention_launch", _I32, [_P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_set_timing", _I32, [_I32]),
     ("dsa_topk_indexer_kernel_ms", _I32, [ctypes.POINTER(ctypes.c_float)]),
 ]

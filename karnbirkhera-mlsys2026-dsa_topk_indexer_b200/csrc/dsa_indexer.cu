@@ -18,6 +18,7 @@
 #include "indexer_kernel.cuh"
 #include "segment_kernels.cuh"
 #include "cache_writer.cuh"
+#include "sparse_attention.cuh"
 
 namespace dsa {
 
@@ -183,7 +184,9 @@ int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
         cudaFuncSetAttribute(reinterpret_cast<const void*>(&cache_write_kernel<true>),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<true>::kSmem) != cudaSuccess ||
         cudaFuncSetAttribute(reinterpret_cast<const void*>(&cache_write_kernel<false>),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<false>::kSmem) != cudaSuccess)
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<false>::kSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&sparse_attention_kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, SaLayout::kBytes) != cudaSuccess)
       return DSA_ERR_CUDA;
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_stream_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kS_SmemBytes) != cudaSuccess ||
@@ -822,6 +825,137 @@ extern "C" int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* 
     cache_write_kernel<false><<<static_cast<unsigned>(blocks), 32 * kWriterWarps, WriterGeom<false>::kSmem, st>>>(
         k, slots, static_cast<uint8_t*>(k_cache), num_tokens, num_pages);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 1;
+  return DSA_OK;
+}
+
+// ------------------------------------------------------- sparse attention
+namespace dsa {
+namespace {
+
+// Split-combine buffers of the sparse attention, one set per (device,
+// stream): partial outputs and (max, sum) per split, and one counter per
+// token that must be zero between launches (zeroed here when allocated, reset
+// by the kernel after each use). Grown outside stream capture only; replaced
+// buffers are kept because work queued earlier may still use them.
+struct AttnWorkspace {
+  void* parts = nullptr;
+  size_t part_bytes = 0;
+  uint32_t* counters = nullptr;
+  int64_t ncounters = 0;
+};
+std::map<std::pair<int, cudaStream_t>, AttnWorkspace> g_attn_ws;
+
+int attn_workspace(cudaStream_t stream, size_t part_bytes, int64_t ncounters, void** parts, uint32_t** counters) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  AttnWorkspace& ws = g_attn_ws[{dev, stream}];
+  if (ws.part_bytes < part_bytes || ws.ncounters < ncounters) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+      return DSA_ERR_CUDA;  // first use of this size must happen outside capture
+  }
+  if (ws.part_bytes < part_bytes) {
+    size_t want = part_bytes < 2 * ws.part_bytes ? 2 * ws.part_bytes : part_bytes;
+    void* fresh = nullptr;
+    if (cudaMalloc(&fresh, want) != cudaSuccess) return DSA_ERR_CUDA;
+    if (ws.parts) g_retired.push_back(ws.parts);
+    ws.parts = fresh;
+    ws.part_bytes = want;
+  }
+  if (ws.ncounters < ncounters) {
+    int64_t want = ncounters < 2 * ws.ncounters ? 2 * ws.ncounters : ncounters;
+    if (want < 1024) want = 1024;
+    void* fresh = nullptr;
+    if (cudaMalloc(&fresh, static_cast<size_t>(want) * 4) != cudaSuccess) return DSA_ERR_CUDA;
+    if (cudaMemsetAsync(fresh, 0, static_cast<size_t>(want) * 4, stream) != cudaSuccess) return DSA_ERR_CUDA;
+    if (ws.counters) g_retired.push_back(ws.counters);
+    ws.counters = static_cast<uint32_t*>(fresh);
+    ws.ncounters = want;
+  }
+  *parts = ws.parts;
+  *counters = ws.counters;
+  return DSA_OK;
+}
+
+// Splits of each token's index list: the count that minimises
+// waves x (tiles per CTA + one tile's worth for the partial's round trip)
+// + the combine (one CTA reads all S partials of 32 KB, about S / 12 of a
+// tile's gather time), one CTA per SM; ties go to fewer splits. Each split
+// holds at most kSaMaxChunk entries.
+int choose_splits(int64_t tokens, int64_t ntiles, int num_sms) {
+  const int64_t min_s = (ntiles * kSaTile + kSaMaxChunk - 1) / kSaMaxChunk;
+  int best = static_cast<int>(min_s < 1 ? 1 : min_s);
+  double best_cost = -1.0;
+  for (int64_t s = best; s <= kSaMaxSplits && s <= (ntiles < 1 ? 1 : ntiles); ++s) {
+    const int64_t per = (ntiles + s - 1) / s;
+    const int64_t used = (ntiles + per - 1) / per;  // splits that hold a tile
+    if (used != s) continue;
+    const int64_t waves = (tokens * s + num_sms - 1) / num_sms;
+    const double cost = static_cast<double>(waves) * static_cast<double>(per + (s > 1 ? 1 : 0)) +
+                        (s > 1 ? static_cast<double>(s) / 12.0 : 0.0);
+    if (best_cost < 0.0 || cost < best_cost) {
+      best_cost = cost;
+      best = static_cast<int>(s);
+    }
+  }
+  return best;
+}
+
+}  // namespace
+}  // namespace dsa
+
+extern "C" int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe, const void* ckv_cache,
+                                           const void* kpe_cache, const int32_t* sparse_indices, float sm_scale,
+                                           void* output, float* lse, int64_t num_tokens, int64_t num_indices,
+                                           int64_t num_pages, void* stream) {
+  using namespace dsa;
+  t_last_launches = 0;
+  if (num_tokens < 0 || num_indices < 0 || num_pages < 1) return DSA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return DSA_OK;
+  if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !output || !lse || (num_indices > 0 && !sparse_indices))
+    return DSA_ERR_INVALID_ARG;
+  if (num_indices > static_cast<int64_t>(kSaMaxChunk) * kSaMaxSplits) return DSA_ERR_TOO_LARGE;
+  if (!aligned16(q_nope) || !aligned16(q_pe) || !aligned16(ckv_cache) || !aligned16(kpe_cache) ||
+      (reinterpret_cast<uintptr_t>(output) & 3u) || (reinterpret_cast<uintptr_t>(lse) & 3u) ||
+      (reinterpret_cast<uintptr_t>(sparse_indices) & 3u))
+    return DSA_ERR_MISALIGNED;
+  if (num_tokens * kSaMaxSplits > 0x7FFFFFFFll) return DSA_ERR_TOO_LARGE;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t ntiles = (num_indices + kSaTile - 1) / kSaTile;
+  const int splits = choose_splits(num_tokens, ntiles, num_sms);
+  const int64_t per = splits > 1 ? (ntiles + splits - 1) / splits : ntiles;
+  SparseAttnParams prm{};
+  prm.q_nope = static_cast<const __nv_bfloat16*>(q_nope);
+  prm.q_pe = static_cast<const __nv_bfloat16*>(q_pe);
+  prm.ckv = static_cast<const __nv_bfloat16*>(ckv_cache);
+  prm.kpe = static_cast<const __nv_bfloat16*>(kpe_cache);
+  prm.indices = sparse_indices;
+  prm.out = static_cast<__nv_bfloat16*>(output);
+  prm.lse = lse;
+  prm.num_slots = num_pages * 64;
+  prm.num_indices = static_cast<int32_t>(num_indices);
+  prm.splits = splits;
+  prm.chunk = static_cast<int32_t>((per < 1 ? 1 : per) * kSaTile);
+  prm.scale_log2 = static_cast<float>(static_cast<double>(sm_scale) * 1.4426950408889634);
+  if (splits > 1) {
+    void* parts = nullptr;
+    uint32_t* counters = nullptr;
+    const size_t part_bytes = static_cast<size_t>(num_tokens) * splits * kSaHeads * (kSaCkv + 2) * sizeof(float);
+    rc = attn_workspace(st, part_bytes, num_tokens, &parts, &counters);
+    if (rc != DSA_OK) return rc;
+    prm.part_o = static_cast<float*>(parts);
+    prm.part_ml = prm.part_o + static_cast<size_t>(num_tokens) * splits * kSaHeads * kSaCkv;
+    prm.counters = counters;
+  }
+  KernelTimer timer(st);
+  sparse_attention_kernel<<<static_cast<unsigned>(num_tokens * splits), kSaThreads, SaLayout::kBytes, st>>>(prm);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  timer.stop();
   t_last_launches = 1;
   return DSA_OK;
 }

@@ -116,3 +116,47 @@ def cache_write(k, slots, k_cache):
         flat[page, off * 128:(off + 1) * 128] = q[t]
         flat[page, 8192 + off * 4:8192 + off * 4 + 4] = scale[t:t + 1].view(torch.uint8)
     return k_cache
+
+
+def sparse_attention(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scale, chunk=8):
+    """CPU restatement of the sparse MLA attention that consumes the
+    indexer's topk_indices (operator dsa_sparse_attention_h16_ckv512_kpe64_
+    topk2048_ps64, named at FAQ.md:83 and EVALUATION.md:54-57,87 of the
+    reference, which holds no code, definition or fixture for it; its
+    grader-side definition lives in the contest dataset, absent here, so
+    this restatement is unpinned). Test infrastructure only.
+
+    Absorbed multi-head latent attention over the selected slots, per token
+    t and head h, in fp64 over the bf16 inputs:
+      logits_j = (q_nope[t,h] . ckv[s_j] + q_pe[t,h] . kpe[s_j]) * sm_scale
+      out[t,h] = softmax(logits) @ ckv[s]            (values = the latent rows)
+      lse[t,h] = log(sum_j exp(logits_j)) / log(2)   (base 2)
+    for the entries s_j >= 0 of sparse_indices[t] (slot = page*64+offset into
+    the [pages, 64, D] pools). No valid entry: out = 0, lse = -inf.
+    Returns (out float32 [T,16,512], lse float32 [T,16])."""
+    T, H, Dc = q_nope.shape
+    ckv = ckv_cache.reshape(-1, ckv_cache.shape[-1])
+    kpe = kpe_cache.reshape(-1, kpe_cache.shape[-1])
+    out = torch.zeros(T, H, Dc, dtype=torch.float32)
+    lse = torch.full((T, H), float("-inf"), dtype=torch.float32)
+    n_slots = ckv.shape[0]
+    for s in range(0, T, chunk):
+        e = min(T, s + chunk)
+        idx = sparse_indices[s:e].long()
+        valid = (idx >= 0) & (idx < n_slots)
+        safe = torch.where(valid, idx, torch.zeros_like(idx))
+        kc = ckv[safe].to(torch.float64)                 # [c, L, 512]
+        kp = kpe[safe].to(torch.float64)                 # [c, L, 64]
+        logits = (torch.einsum("chd,cld->chl", q_nope[s:e].to(torch.float64), kc) +
+                  torch.einsum("chd,cld->chl", q_pe[s:e].to(torch.float64), kp)) * float(sm_scale)
+        logits = logits.masked_fill(~valid[:, None, :], float("-inf"))
+        any_valid = valid.any(dim=1)
+        m = logits.amax(dim=2, keepdim=True)
+        m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+        p = torch.exp(logits - m)
+        den = p.sum(dim=2, keepdim=True)
+        o = torch.einsum("chl,cld->chd", p, kc) / torch.where(den > 0, den, torch.ones_like(den))
+        lse_c = (torch.log(den[..., 0]) + m[..., 0]) / torch.log(torch.tensor(2.0, dtype=torch.float64))
+        out[s:e] = torch.where(any_valid[:, None, None], o, torch.zeros_like(o)).to(torch.float32)
+        lse[s:e] = torch.where(any_valid[:, None], lse_c, torch.full_like(lse_c, float("-inf"))).to(torch.float32)
+    return out, lse
