@@ -55,6 +55,21 @@ KEY_SHARDED_CONFIGS = (4,)
 FLOP_PER_KEY = 64 * 128 * 2  # one query row against one key: 64 heads x 128-dim dot products
 
 
+class L2Flush:
+    """Empties L2 of the step's data before every timed step by writing a
+    256 MB buffer (more than the 126 MB L2). The write leaves dirty lines in
+    L2 whose write-back overlaps the timed step; that cost is kept (reading
+    another buffer afterwards removes it on large steps but slowed the B=1
+    decode call by ~10 us, so the plain write is the measurement)."""
+    NOTE = "flushed (256 MB write) before every timed step"
+
+    def __init__(self, torch, dev):
+        self.w = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+
+
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -181,7 +196,7 @@ def main():
     w = wl.config(args.config, device=dev, seed=seed, scale_batch=args.batch_scale)
     B = w.batch
     out = torch.empty((B, 2048), dtype=torch.int32, device=dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
+    flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream(dev)
 
     if key_sharded:
@@ -219,7 +234,7 @@ def main():
     cap_stream.wait_stream(stream)
     with torch.cuda.stream(cap_stream):
         for _ in range(args.warmup):
-            flush.zero_()
+            flush()
             call()
     torch.cuda.synchronize()
     pkg.device_status(local, clear=True)
@@ -246,7 +261,7 @@ def main():
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
-            flush.zero_()
+            flush()
             starts[i].record(stream)
             if graph is not None:
                 graph.replay()
@@ -267,7 +282,7 @@ def main():
     pkg.set_kernel_timing(True)
     kms = []
     for i in range(args.steps):
-        flush.zero_()
+        flush()
         call()
         kms.append(pkg.last_kernel_ms())
     pkg.set_kernel_timing(False)
@@ -308,7 +323,7 @@ def main():
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(3):
-        flush.zero_()
+        flush()
         e2e_call()
     torch.cuda.synchronize()
     es = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -316,7 +331,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     for i in range(args.steps):
-        flush.zero_()
+        flush()
         es[i].record(stream)
         e2e_call()
         ee[i].record(stream)
@@ -381,7 +396,7 @@ def main():
                                        f"key-sharded x{world} (NCCL all-gather of candidate lists + merge)")
                        if key_sharded
                        else f"request-sharded x{world}",
-                       "l2": "flushed (256 MB write) before every timed step"},
+                       "l2": L2Flush.NOTE},
             "e2e": {"value": B * (1 if key_sharded else world) / (e2e_max * 1e-3), "unit": "queries/s",
                     "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max,
@@ -417,16 +432,16 @@ def cache_write_bench(args, rank, local):
     k = (torch.randn((T, 128), generator=g, device=dev) * 0.5).to(torch.bfloat16)
     slots = torch.randperm(pages * 64, generator=g, device=dev)[:T].to(torch.int64)
     cache = torch.zeros((pages, 64, 1, 132), dtype=torch.uint8, device=dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(torch, dev)
     for _ in range(max(3, args.warmup)):
-        flush.zero_()
+        flush()
         pkg.index_cache_write(k, slots, cache)
     torch.cuda.synchronize()
     st = torch.cuda.current_stream(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         for a, b in ev:
-            flush.zero_()
+            flush()
             a.record(st)
             pkg.index_cache_write(k, slots, cache)
             b.record(st)
@@ -442,7 +457,7 @@ def cache_write_bench(args, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> fp8_e4m3",
             "data": "synthetic",
             "config": {"workload": f"{T} tokens into {pages} pages, random slot permutation",
-                       "l2": "flushed (256 MB write) before every timed step"},
+                       "l2": L2Flush.NOTE},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "kernel": "dsa::cache_write_kernel<true>"},
@@ -472,7 +487,7 @@ def sparse_attention_bench(args, rank, local):
     out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
     lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
     scale = 1.0 / math.sqrt(192.0)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush = L2Flush(torch, dev)
     st = torch.cuda.current_stream(dev)
     # Warm-up on the capture stream (the library allocates its split buffers
     # for that stream outside capture), then one CUDA graph of the call, so
@@ -481,7 +496,7 @@ def sparse_attention_bench(args, rank, local):
     cap.wait_stream(st)
     with torch.cuda.stream(cap):
         for _ in range(max(3, args.warmup)):
-            flush.zero_()
+            flush()
             pkg.sparse_attention(q_nope, q_pe, ckv, kpe, idx, scale, out, lse)
     torch.cuda.synchronize()
     launches = pkg.last_launch_count()
@@ -492,7 +507,7 @@ def sparse_attention_bench(args, rank, local):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
         for a, b in ev:
-            flush.zero_()
+            flush()
             a.record(st)
             graph.replay()
             b.record(st)
@@ -505,7 +520,7 @@ def sparse_attention_bench(args, rank, local):
     d_qn, d_qp, d_idx = torch.empty_like(q_nope), torch.empty_like(q_pe), torch.empty_like(idx)
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.steps + 3):
-        flush.zero_()
+        flush()
         a, b = ev2[i - 3] if i >= 3 else (None, None)
         if a is not None:
             a.record(st)
@@ -531,7 +546,7 @@ def sparse_attention_bench(args, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)",
             "data": "synthetic",
             "config": {"workload": f"{T} tokens x 2048 slots, 16 heads, ckv 512 + kpe 64, pool {pages} pages",
-                       "l2": "flushed (256 MB write) before every timed step"},
+                       "l2": L2Flush.NOTE},
             "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",

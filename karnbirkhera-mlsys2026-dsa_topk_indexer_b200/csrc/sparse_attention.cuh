@@ -48,6 +48,7 @@ constexpr int kSaWarps = 8;
 constexpr int kSaThreads = 32 * kSaWarps;
 constexpr int kSaMaxChunk = 2048;  // index entries one CTA handles at most
 constexpr int kSaMaxSplits = 32;
+constexpr float kSaSlack = 8.f;    // base-2 headroom of the lazy softmax maximum
 
 struct SaLayout {
   static constexpr int kStage = kSaTile * kSaRowBytes;  // 73,728
@@ -221,39 +222,58 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attention_kernel(const S
     x1 = fmaxf(x1, __shfl_xor_sync(0xFFFFFFFFu, x1, 1));
     x0 = fmaxf(x0, __shfl_xor_sync(0xFFFFFFFFu, x0, 2));
     x1 = fmaxf(x1, __shfl_xor_sync(0xFFFFFFFFu, x1, 2));
-    if (tig == 0) {
-      red[warp * kSaHeads + g] = x0;
-      red[warp * kSaHeads + g + 8] = x1;
+    if (tig == 0) {  // head-major: red[h * 8 + w]
+      red[g * kSaWarps + warp] = x0;
+      red[(g + 8) * kSaWarps + warp] = x1;
     }
-    __syncthreads();
-    float tm0 = -INFINITY, tm1 = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kSaWarps; ++w) {
-      tm0 = fmaxf(tm0, red[w * kSaHeads + g]);
-      tm1 = fmaxf(tm1, red[w * kSaHeads + g + 8]);
-    }
-    const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);
-    const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float a0 = exp2f(m0 - mu0), a1 = exp2f(m1 - mu1);
-    m0 = mn0;
-    m1 = mn1;
-    const float p0 = exp2f(s[0] - mu0), p1 = exp2f(s[1] - mu0);
-    const float p2 = exp2f(s[2] - mu1), p3 = exp2f(s[3] - mu1);
-    l0 = l0 * a0 + p0 + p1;
-    l1 = l1 * a1 + p2 + p3;
+    // Lazy reference maximum (base 2, per head, identical in every warp): it
+    // only moves when a tile's maximum exceeds it by more than kSaSlack, so
+    // p = 2^(s - m) stays <= 2^kSaSlack and most tiles need neither the
+    // rescale of O and l nor a second barrier. P is first computed with the
+    // current reference; if any head moves, every warp (all read the same
+    // maxima) recomputes and rewrites it behind one more barrier.
+    const float mu0 = m0 == -INFINITY ? 0.f : m0, mu1 = m1 == -INFINITY ? 0.f : m1;
+    float p0 = exp2f(s[0] - mu0), p1 = exp2f(s[1] - mu0);
+    float p2 = exp2f(s[2] - mu1), p3 = exp2f(s[3] - mu1);
     // P fragment of k-block w/2: even warps hold its keys 0..7 (a0, a1),
     // odd warps its keys 8..15 (a2, a3).
-    reinterpret_cast<uint2*>(pfrag + (warp >> 1) * 32 + lane)[warp & 1] =
-        make_uint2(pack_bf16x2(p0, p1), pack_bf16x2(p2, p3));
+    uint2* pslot = reinterpret_cast<uint2*>(pfrag + (warp >> 1) * 32 + lane) + (warp & 1);
+    *pslot = make_uint2(pack_bf16x2(p0, p1), pack_bf16x2(p2, p3));
     __syncthreads();
-
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      o[nb][0] *= a0;
-      o[nb][1] *= a0;
-      o[nb][2] *= a1;
-      o[nb][3] *= a1;
+    float tm0, tm1;
+    {
+      const float4* r0 = reinterpret_cast<const float4*>(red + g * kSaWarps);
+      const float4* r1 = reinterpret_cast<const float4*>(red + (g + 8) * kSaWarps);
+      const float4 u0 = r0[0], u1 = r0[1], w0 = r1[0], w1 = r1[1];
+      tm0 = fmaxf(fmaxf(fmaxf(u0.x, u0.y), fmaxf(u0.z, u0.w)), fmaxf(fmaxf(u1.x, u1.y), fmaxf(u1.z, u1.w)));
+      tm1 = fmaxf(fmaxf(fmaxf(w0.x, w0.y), fmaxf(w0.z, w0.w)), fmaxf(fmaxf(w1.x, w1.y), fmaxf(w1.z, w1.w)));
     }
+    const bool up0 = tm0 > m0 + kSaSlack, up1 = tm1 > m1 + kSaSlack;
+    if (__any_sync(0xFFFFFFFFu, up0 || up1)) {  // uniform across the CTA
+      const float mn0 = up0 ? tm0 : m0, mn1 = up1 ? tm1 : m1;
+      const float nu0 = mn0 == -INFINITY ? 0.f : mn0, nu1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float a0 = exp2f(m0 - nu0), a1 = exp2f(m1 - nu1);
+      m0 = mn0;
+      m1 = mn1;
+      p0 = exp2f(s[0] - nu0);
+      p1 = exp2f(s[1] - nu0);
+      p2 = exp2f(s[2] - nu1);
+      p3 = exp2f(s[3] - nu1);
+      l0 *= a0;
+      l1 *= a1;
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+        o[nb][0] *= a0;
+        o[nb][1] *= a0;
+        o[nb][2] *= a1;
+        o[nb][3] *= a1;
+      }
+      *pslot = make_uint2(pack_bf16x2(p0, p1), pack_bf16x2(p2, p3));  // own slot only
+      __syncthreads();  // the rewritten P is visible before any warp's P V
+    }
+    l0 += p0 + p1;
+    l1 += p2 + p3;
+
 #pragma unroll
     for (int kb = 0; kb < 4; ++kb) {
       const uint4 af4 = pfrag[kb * 32 + lane];
@@ -271,9 +291,9 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attention_kernel(const S
     }
   }
   ptx::cp_async_wait_all();
+  __syncthreads();  // every warp is done with red and the ring
 
-  // Sums over the whole split: quad, then warps (red is free: every warp has
-  // passed the last P barrier, after its last read of red).
+  // Sums over the whole split: quad, then warps.
   l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 1);
   l1 += __shfl_xor_sync(0xFFFFFFFFu, l1, 1);
   l0 += __shfl_xor_sync(0xFFFFFFFFu, l0, 2);
