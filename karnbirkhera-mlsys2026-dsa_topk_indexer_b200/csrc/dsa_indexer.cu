@@ -885,6 +885,7 @@ int attn_workspace(cudaStream_t stream, size_t part_bytes, int64_t ncounters, vo
 // tile's gather time), one CTA per SM; ties go to fewer splits. Each split
 // holds at most kSaMaxChunk entries.
 int choose_splits(int64_t tokens, int64_t ntiles, int num_sms) {
+  if (ntiles <= 1) return 1;  // an empty or one-tile list is never split
   const int64_t min_s = (ntiles * kSaTile + kSaMaxChunk - 1) / kSaMaxChunk;
   int best = static_cast<int>(min_s < 1 ? 1 : min_s);
   double best_cost = -1.0;

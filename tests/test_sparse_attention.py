@@ -135,7 +135,8 @@ def _check(q_nope, q_pe, ckv, kpe, idx, scale=SM_SCALE):
 @pytest.mark.parametrize("T", [1, 7, 64, 148, 300])
 def test_gpu_matches_oracle_full_lists(T):
     # 148 tokens (one per SM) run one CTA per token; the others split every
-    # list (32, 16, 2 and 4 ways) and combine on the device.
+    # list across CTAs (1 and 7 tokens many ways, 64 and 300 two and four
+    # ways) and combine on the device.
     _check(*_inputs(T, 2048, 2000, 10 + T))
 
 
@@ -187,3 +188,46 @@ def test_gpu_indexer_then_attention_chain():
     assert int((topk[0] >= 0).sum()) == 1500 and int((topk[3] >= 0).sum()) == 2048
     q_nope, q_pe, ckv, kpe, _ = _inputs(w.batch, 1, w.num_pages, 7)
     _check(q_nope, q_pe, ckv, kpe, topk)
+
+
+@pytest.mark.gpu
+def test_gpu_empty_lists():
+    # L = 0: every token has no slot (output 0, lse -inf); T = 0 is a no-op.
+    q_nope, q_pe, ckv, kpe, _ = _inputs(5, 1, 8, 30)
+    out, lse = _run_gpu(q_nope, q_pe, ckv, kpe, torch.empty((5, 0), dtype=torch.int32))
+    assert torch.all(out == 0) and torch.all(torch.isneginf(lse))
+    pkg = package()
+    d = torch.device("cuda:0")
+    e_out, e_lse = pkg.sparse_attention(q_nope[:0].to(d), q_pe[:0].to(d), ckv.to(d), kpe.to(d),
+                                        torch.empty((0, 2048), dtype=torch.int32, device=d), SM_SCALE)
+    torch.cuda.synchronize()
+    assert e_out.shape == (0, 16, 512) and e_lse.shape == (0, 16)
+
+
+@pytest.mark.gpu
+def test_gpu_graph_capture_after_warmup():
+    """A split shape is warmed up on a stream (the library allocates its
+    split buffers there), captured into a CUDA graph, and replayed on new
+    inputs copied into the same buffers: replays equal direct calls."""
+    pkg = package()
+    d = torch.device("cuda:0")
+    a = [t.to(d) for t in _inputs(6, 2048, 500, 40)]   # 6 tokens: lists split across CTAs
+    b = [t.to(d) for t in _inputs(6, 2048, 500, 41)]
+    bufs = [t.clone() for t in a]                       # the graph's input buffers
+    s = torch.cuda.Stream(d)
+    s.wait_stream(torch.cuda.current_stream(d))
+    with torch.cuda.stream(s):
+        out, lse = pkg.sparse_attention(*bufs, SM_SCALE)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        pkg.sparse_attention(*bufs, SM_SCALE, output=out, lse=lse)
+    for src in (b, a, b):
+        for dst_t, src_t in zip(bufs, src):
+            dst_t.copy_(src_t)
+        g.replay()
+        torch.cuda.synchronize()
+        want = pkg.sparse_attention(*src, SM_SCALE)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want[0]) and torch.equal(lse, want[1])
+    del g
