@@ -149,6 +149,25 @@ def cpu_reference_run(w, budget_s, max_queries=None):
     return done / dt, done, dt, threads, passes
 
 
+def cpu_port_rate(fn, units_per_call, budget_s):
+    """Times fn() (a call of the CPU restatement in oracle/reference_torch.py
+    on a bounded sample covering `units_per_call` units) until about
+    `budget_s` seconds have run, on all host threads. Returns (units/s,
+    threads, calls)."""
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    calls = 0
+    t0 = time.perf_counter()
+    while True:
+        fn()
+        calls += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s:
+            break
+    return units_per_call * calls / dt, threads, calls
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,6 +466,17 @@ def cache_write_bench(args, rank, local):
             b.record(st)
         torch.cuda.synchronize()
     ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    cpu = None
+    if not args.no_cpu_baseline:
+        # The reference has no writer; the CPU restatement on 65536 tokens.
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import reference_torch as rt  # CPU baseline only
+        n = min(T, 65536)
+        ks, ss = k[:n].cpu(), slots[:n].cpu() % (((n + 63) // 64) * 64)
+        cc = torch.zeros(((n + 63) // 64, 64, 1, 132), dtype=torch.uint8)
+        rate, threads, calls = cpu_port_rate(lambda: rt.cache_write(ks, ss, cc), n, 10.0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{n} tokens per call, {calls} calls (oracle/reference_torch.py cache_write)"}
     hbm, _, peak_src = peaks()
     algo = T * (256 + 8 + 132)
     achieved = algo / (ms * 1e-3) / 1e9
@@ -461,7 +491,7 @@ def cache_write_bench(args, rank, local):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "kernel": "dsa::cache_write_kernel<true>"},
-            "gpu_launches": args.steps, "clocks": clk.summary()}), flush=True)
+            "gpu_launches": args.steps, "clocks": clk.summary(), "cpu_baseline": cpu}), flush=True)
 
 
 def sparse_attention_bench(args, rank, local):
@@ -536,6 +566,19 @@ def sparse_attention_bench(args, rank, local):
     ms_e2e = sum(a.elapsed_time(b) for a, b in ev2) / args.steps
     h2d = h_qn.numel() * 2 + h_qp.numel() * 2 + h_idx.numel() * 4
     d2h = h_out.numel() * 2 + h_lse.numel() * 4
+    cpu = None
+    if not args.no_cpu_baseline:
+        # The reference has no code for this operator; the CPU restatement on
+        # 8 tokens of the same workload.
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import reference_torch as rt  # CPU baseline only
+        n = min(T, 8)
+        c_qn, c_qp, c_ix = q_nope[:n].cpu(), q_pe[:n].cpu(), idx[:n].cpu()
+        c_ckv, c_kpe = ckv.cpu(), kpe.cpu()
+        rate, threads, calls = cpu_port_rate(lambda: rt.sparse_attention(c_qn, c_qp, c_ckv, c_kpe, c_ix, scale),
+                                             n, 10.0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{n} tokens x 2048 slots per call, {calls} calls (oracle/reference_torch.py sparse_attention)"}
     hbm, _, peak_src = peaks()
     algo = T * (L * 1152 + 16 * 576 * 2 + 16 * 512 * 2 + 16 * 4 + L * 4)
     achieved = algo / (ms * 1e-3) / 1e9
@@ -552,7 +595,7 @@ def sparse_attention_bench(args, rank, local):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "kernel": "dsa::sparse_attention_kernel"},
-            "gpu_launches": args.steps * launches, "clocks": clk.summary()}), flush=True)
+            "gpu_launches": args.steps * launches, "clocks": clk.summary(), "cpu_baseline": cpu}), flush=True)
 
 
 def reference_arm(args, rank, wl):
