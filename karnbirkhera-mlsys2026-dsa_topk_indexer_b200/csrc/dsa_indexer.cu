@@ -881,11 +881,21 @@ int attn_workspace(cudaStream_t stream, size_t part_bytes, int64_t ncounters, vo
 
 // Splits of each token's index list: the count that minimises
 // waves x (tiles per CTA + one tile's worth for the partial's round trip)
-// + the combine (one CTA reads all S partials of 32 KB, about S / 12 of a
-// tile's gather time), one CTA per SM; ties go to fewer splits. Each split
+// + the combine (one CTA pulls all S partials of 32 KB, about a quarter of a
+// tile's time each), one CTA per SM; ties go to fewer splits. Each split
 // holds at most kSaMaxChunk entries.
 int choose_splits(int64_t tokens, int64_t ntiles, int num_sms) {
   if (ntiles <= 1) return 1;  // an empty or one-tile list is never split
+  // DSA_SA_SPLITS=<n> forces n splits when that is a valid split of the list
+  // (tuning and tests).
+  if (const char* env = std::getenv("DSA_SA_SPLITS")) {
+    const int64_t s = std::atoi(env);
+    const int64_t min_s = (ntiles * kSaTile + kSaMaxChunk - 1) / kSaMaxChunk;
+    if (s >= min_s && s >= 1 && s <= kSaMaxSplits && s <= ntiles) {
+      const int64_t per = (ntiles + s - 1) / s;
+      if ((ntiles + per - 1) / per == s) return static_cast<int>(s);
+    }
+  }
   const int64_t min_s = (ntiles * kSaTile + kSaMaxChunk - 1) / kSaMaxChunk;
   int best = static_cast<int>(min_s < 1 ? 1 : min_s);
   double best_cost = -1.0;
@@ -895,7 +905,7 @@ int choose_splits(int64_t tokens, int64_t ntiles, int num_sms) {
     if (used != s) continue;
     const int64_t waves = (tokens * s + num_sms - 1) / num_sms;
     const double cost = static_cast<double>(waves) * static_cast<double>(per + (s > 1 ? 1 : 0)) +
-                        (s > 1 ? static_cast<double>(s) / 12.0 : 0.0);
+                        (s > 1 ? static_cast<double>(s) / 4.0 : 0.0);
     if (best_cost < 0.0 || cost < best_cost) {
       best_cost = cost;
       best = static_cast<int>(s);

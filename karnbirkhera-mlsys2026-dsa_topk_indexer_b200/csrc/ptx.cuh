@@ -298,6 +298,15 @@ __device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void* src, u
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// GPU-scope atomic add with acquire-release semantics: publishes the writes
+// that happen before it (a CTA's, when issued after a barrier) and acquires
+// those published by earlier releases on the same word.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");

@@ -48,6 +48,7 @@ constexpr int kSaWarps = 8;
 constexpr int kSaThreads = 32 * kSaWarps;
 constexpr int kSaMaxChunk = 2048;  // index entries one CTA handles at most
 constexpr int kSaMaxSplits = 32;
+constexpr int kSaCombineParts = 4;  // partials per round of the split combine (128 KB)
 constexpr float kSaSlack = 8.f;    // base-2 headroom of the lazy softmax maximum
 
 struct SaLayout {
@@ -62,7 +63,8 @@ struct SaLayout {
 static_assert(SaLayout::kBytes <= 232448, "sparse attention shared memory above the per-CTA limit");
 static_assert(kSaHeads * kSaRowBytes <= SaLayout::kStage, "Q must fit in one stage");
 static_assert(kSaTile * kSaRowChunks % kSaThreads == 0, "gather chunks must split evenly");
-static_assert(kSaMaxSplits * kSaHeads * 4 <= SaLayout::kStage, "combine weights live in stage 0");
+static_assert(kSaMaxSplits * kSaHeads * 12 <= SaLayout::kStage, "combine weights and partial (max, sum) live in stage 0");
+static_assert(kSaCombineParts * kSaHeads * kSaCkv * 4 <= 2 * SaLayout::kStage, "a combine round fits in stages 1-2");
 
 struct SparseAttnParams {
   const __nv_bfloat16* q_nope;  // [T, 16, 512]
@@ -341,24 +343,33 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attention_kernel(const S
       *reinterpret_cast<float2*>(pm + 2 * (g + 8)) = make_float2(m1, L1);
     }
   }
-  __threadfence();
+  // One thread's acquire-release add after the barrier publishes the whole
+  // CTA's partial and, for the last arriving split, acquires every other
+  // split's (the barrier below extends that to all threads), instead of a
+  // sequentially consistent fence in every thread.
   __syncthreads();
-  if (tid == 0) misc[1] = atomicAdd(&p.counters[t], 1u) == static_cast<uint32_t>(p.splits - 1);
+  if (tid == 0)
+    misc[1] = ptx::atom_add_acq_rel_gpu(&p.counters[t], 1u) == static_cast<uint32_t>(p.splits - 1);
   __syncthreads();
   if (!misc[1]) return;
   // Last split of this token: every other split's partial is visible.
-  __threadfence();
   if (tid == 0) p.counters[t] = 0u;
   const int S = p.splits;
   const int64_t first = t * S;
-  float* wgt = reinterpret_cast<float*>(sm);  // [S][16] weight of each partial
+  float* wgt = reinterpret_cast<float*>(sm);                          // [S][16] weight of each partial
+  float2* mls = reinterpret_cast<float2*>(sm + kSaMaxSplits * kSaHeads * 4);  // [S][16] (max, sum)
+  // Every partial's (max, sum) in one round of loads (a loop over S in 16
+  // threads would wait for each load in turn).
+  for (int e = tid; e < S * kSaHeads; e += kSaThreads)
+    mls[e] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + first * kSaHeads + e);
+  __syncthreads();
   if (tid < kSaHeads) {
     const int h = tid;
     float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(p.part_ml + ((first + s2) * kSaHeads + h) * 2));
+    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, mls[s2 * kSaHeads + h].x);
     float L = 0.f;
     for (int s2 = 0; s2 < S; ++s2) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + ((first + s2) * kSaHeads + h) * 2));
+      const float2 ml = mls[s2 * kSaHeads + h];
       const float e = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
       wgt[s2 * kSaHeads + h] = e;
       L += e * ml.y;
@@ -367,54 +378,43 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attention_kernel(const S
     for (int s2 = 0; s2 < S; ++s2) wgt[s2 * kSaHeads + h] *= inv;
     p.lse[t * kSaHeads + h] = L > 0.f ? M + log2f(L) : -INFINITY;
   }
-  __syncthreads();
-  // Thread: head tid / 16, value columns 32 (tid % 16) .. +32 (eight float4
-  // per partial); partials are read four at a time (32 loads in flight).
-  {
-    const int h = tid >> 4, d0 = (tid & 15) * 32;
-    float acc[32];
+  // The partials (32 KB each) come in with cp.async, kSaCombineParts per
+  // round, into the ring's stages 1-2 (plain loads from one SM keep too few
+  // bytes in flight: ~18 GB/s). Thread tid owns float4 e = tid + 256 k
+  // (k < 8) of the [16 heads x 128 float4] output, so every warp reads and
+  // writes 512 contiguous bytes.
+  float4 acc[8];
 #pragma unroll
-    for (int e = 0; e < 32; ++e) acc[e] = 0.f;
-    const float* base = p.part_o + (first * kSaHeads + h) * kSaCkv + d0;
-    const int64_t pstride = static_cast<int64_t>(kSaHeads) * kSaCkv;
-    int s2 = 0;
+  for (int k = 0; k < 8; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const uint32_t cbuf = sbase + SaLayout::kStage;
+  const float4* cb = reinterpret_cast<const float4*>(sm + SaLayout::kStage);
+  const uint8_t* parts = reinterpret_cast<const uint8_t*>(p.part_o + first * kSaHeads * kSaCkv);
 #pragma unroll 1
-    for (; s2 + 4 <= S; s2 += 4) {
-      float4 v[4][8];
+  for (int s0 = 0; s0 < S; s0 += kSaCombineParts) {
+    const int np = min(kSaCombineParts, S - s0);
+    __syncthreads();  // the weights are visible; the previous round's buffer is read
+    for (int c = tid; c < np * (kSaHeads * kSaCkv / 4); c += kSaThreads)
+      ptx::cp_async16(cbuf + c * 16, parts + (static_cast<int64_t>(s0) * (kSaHeads * kSaCkv / 4) + c) * 16, 16u);
+    ptx::cp_async_commit();
+    ptx::cp_async_wait_all();
+    __syncthreads();
+    for (int q = 0; q < np; ++q) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int f = 0; f < 8; ++f) v[u][f] = __ldcg(reinterpret_cast<const float4*>(base + (s2 + u) * pstride) + f);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = wgt[(s2 + u) * kSaHeads + h];
-#pragma unroll
-        for (int f = 0; f < 8; ++f) {
-          acc[4 * f] += w * v[u][f].x;
-          acc[4 * f + 1] += w * v[u][f].y;
-          acc[4 * f + 2] += w * v[u][f].z;
-          acc[4 * f + 3] += w * v[u][f].w;
-        }
+      for (int k = 0; k < 8; ++k) {
+        const int e = tid + kSaThreads * k;
+        const float w = wgt[(s0 + q) * kSaHeads + (e >> 7)];
+        const float4 v = cb[q * (kSaHeads * kSaCkv / 4) + e];
+        acc[k].x += w * v.x;
+        acc[k].y += w * v.y;
+        acc[k].z += w * v.z;
+        acc[k].w += w * v.w;
       }
     }
-#pragma unroll 1
-    for (; s2 < S; ++s2) {
-      const float w = wgt[s2 * kSaHeads + h];
-#pragma unroll
-      for (int f = 0; f < 8; ++f) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(base + s2 * pstride) + f);
-        acc[4 * f] += w * v.x;
-        acc[4 * f + 1] += w * v.y;
-        acc[4 * f + 2] += w * v.z;
-        acc[4 * f + 3] += w * v.w;
-      }
-    }
-    uint4* dst = reinterpret_cast<uint4*>(p.out + (t * kSaHeads + h) * kSaCkv + d0);
-#pragma unroll
-    for (int f = 0; f < 4; ++f)
-      dst[f] = make_uint4(pack_bf16x2(acc[8 * f], acc[8 * f + 1]), pack_bf16x2(acc[8 * f + 2], acc[8 * f + 3]),
-                          pack_bf16x2(acc[8 * f + 4], acc[8 * f + 5]), pack_bf16x2(acc[8 * f + 6], acc[8 * f + 7]));
   }
+  uint2* dst = reinterpret_cast<uint2*>(p.out + t * kSaHeads * kSaCkv);
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    dst[tid + kSaThreads * k] = make_uint2(pack_bf16x2(acc[k].x, acc[k].y), pack_bf16x2(acc[k].z, acc[k].w));
 }
 
 }  // namespace dsa
