@@ -62,7 +62,8 @@ struct SaLayout {
 };
 static_assert(SaLayout::kBytes <= 232448, "sparse attention shared memory above the per-CTA limit");
 static_assert(kSaHeads * kSaRowBytes <= SaLayout::kStage, "Q must fit in one stage");
-static_assert(kSaTile * kSaRowChunks % kSaThreads == 0, "gather chunks must split evenly");
+static_assert(kSaThreads / 8 * 2 == kSaTile, "the gather runs eight threads per key in two passes over a tile");
+static_assert(kSaRowChunks == 9 * 8, "a key's row is 8 x 128 bytes of ckv and 128 bytes of kpe");
 static_assert(kSaMaxSplits * kSaHeads * 12 <= SaLayout::kStage, "combine weights and partial (max, sum) live in stage 0");
 static_assert(kSaCombineParts * kSaHeads * kSaCkv * 4 <= 2 * SaLayout::kStage, "a combine round fits in stages 1-2");
 
