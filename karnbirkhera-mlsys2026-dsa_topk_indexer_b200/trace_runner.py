@@ -1,28 +1,27 @@
 """Runs the indexer over a directory of FlashInfer-Bench workload files.
 
-    python -m <package>.trace_runner DIR [--k-init normal|randint] [--check] [--iters N]
+    python -m <package>.trace_runner DIR [--k-init normal|randint] [--iters N]
 
 Every `*.safetensors` file in DIR (structural tensors block_table and
 seq_lens, see workloads.load_safetensors_workload) becomes one workload;
 q, weights and the K pages are synthesised. For each workload the indexer
-runs on the current GPU; the output prints one JSON line with the shapes, the
-median device time over N calls (CUDA events) and, with --check, the result
-of the parity rule against the CPU oracle (oracle/, present in a source
-checkout only; test infrastructure).
+runs on the current GPU; the output prints one JSON line with the shapes and
+the median device time over N calls (CUDA events). `main(..., on_result=f)`
+calls f(workload, topk_indices_on_host, record) for each workload before the
+line is printed (tests/check_traces.py uses it to check every result against
+the CPU oracle).
 """
 import argparse
 import glob
 import importlib
 import json
 import os
-import sys
 
 
-def main(argv=None):
+def main(argv=None, on_result=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("dir")
     ap.add_argument("--k-init", choices=["normal", "randint"], default="normal")
-    ap.add_argument("--check", action="store_true")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--seed", type=int, default=0)
     args = ap.parse_args(argv)
@@ -50,19 +49,8 @@ def main(argv=None):
         rec = {"workload": w.name, "batch": w.batch, "max_num_pages": w.max_pages, "num_pages": w.num_pages,
                "visible_keys": w.visible_keys(), "ms_median": sorted(times)[len(times) // 2],
                "schedule": pkg.last_path()}
-        if args.check:
-            root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-            for p in (os.path.join(root, "oracle"), os.path.join(root, "tests")):
-                if p not in sys.path:
-                    sys.path.insert(0, p)
-            import oracle  # test infrastructure: the CPU restatement
-            from parity import check_all
-            ref = oracle.indexer(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
-            sc = oracle.scores(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
-            sl = w.seq_lens.clamp(0, w.max_pages * 64).tolist()
-            fails = check_all(out.cpu().numpy(), ref, [sc[i, :s] for i, s in enumerate(sl)], w.seq_lens.numpy(),
-                              w.block_table.numpy(), w.num_pages)
-            rec["parity"] = "pass" if not fails else f"{len(fails)} failures"
+        if on_result is not None:
+            on_result(w, out.cpu(), rec)
         print(json.dumps(rec), flush=True)
         rows.append(rec)
     return rows
