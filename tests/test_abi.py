@@ -69,3 +69,16 @@ def test_torch_wrapper_validates_before_launch(pkg):
     out = torch.zeros((2, 2048), dtype=torch.int32)
     with pytest.raises(RuntimeError, match="CUDA tensor"):
         pkg.launch_topk_c(q, kc, w, sl, bt, out)
+
+
+def test_missing_library_fails_loudly(monkeypatch):
+    """No CPU fallback: without the built CUDA library every entry point
+    raises instead of computing something else."""
+    import torch
+    pkg = package()
+    monkeypatch.setattr(pkg._lib, "LIB_PATH", os.path.join(ROOT, "no-such-dir", "libdsa_topk_indexer.so"))
+    monkeypatch.setattr(pkg._lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        pkg._lib.load()
+    with pytest.raises(RuntimeError):
+        pkg.last_launch_count()
