@@ -1,5 +1,6 @@
-"""Benchmark of the B200 DSA indexer: queries/s on BASELINE config 1 (decode
-batch, B=64) by default, one JSON line on rank 0.
+"""Benchmark of the B200 DSA indexer: queries/s on BASELINE config 2 (the
+large decode batch the metric is quoted on at 1/2/4/8 B200: 512 requests of
+16k..131k keys) by default, one JSON line on rank 0.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
 
@@ -7,8 +8,10 @@ A step = one indexer call over the whole batch. `value` is device time (CUDA
 events on the launching stream, L2 flushed before every step); `e2e` is the
 same call fed from pinned host buffers (q, weights, seq_lens, block_table
 host->device, top-K device->host inside the timed region; the paged K cache
-is the serving system's resident device state). Under torchrun each rank runs
-its own batch (request sharding, no collective): weak scaling.
+is the serving system's resident device state). Under torchrun the one
+global batch is split: decode configs by request (balanced by total length,
+no collective), the long-context config 4 along the key axis (partial top-K,
+NCCL exchange, merge); both are strong scaling (the global batch is fixed).
 """
 import argparse
 import importlib
@@ -46,8 +49,7 @@ def traffic_per_launch(config, kernel):
     return json.load(open(p)).get(f"cfg{config}:{kernel}")
 
 
-DOMINANT = {"segmented": "dsa::segment_stream_kernel", "cluster": "dsa::indexer_kernel<0>",
-            "cluster-split": "dsa::indexer_kernel<0>"}
+DOMINANT = {"cluster": "dsa::indexer_kernel<0>", "cluster-split": "dsa::indexer_kernel<0>"}
 PREFILL_CONFIGS = (3, 4)
 # Configs whose single sequence is split along the key axis across ranks
 # (every rank holds the same inputs; partial top-K, NCCL all-gather, merge).
@@ -123,24 +125,26 @@ class ClockSampler:
 
 def cpu_reference_run(w, budget_s, max_queries=None):
     """Times the PyTorch CPU restatement of the reference (oracle/
-    reference_torch.py) on a bounded sample of the workload: the first n
-    queries, repeated until about `budget_s` seconds of CPU work have run.
-    Returns (queries/s, queries timed, seconds, threads, passes)."""
+    reference_torch.py) on a bounded sample of the workload: its first n
+    queries (with only the K pages they read, copied to host memory),
+    repeated until about `budget_s` seconds of CPU work have run. Returns
+    (queries/s, queries timed, seconds, threads, passes)."""
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import reference_torch as rt  # CPU baseline only
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cpu = w.to("cpu")
     # probe one query to size the sample
+    one, _ = w.compact([0], "cpu")
     t0 = time.perf_counter()
-    rt.indexer(cpu.q[:1], cpu.k_cache, cpu.weights[:1], cpu.seq_lens[:1], cpu.block_table[:1])
+    rt.indexer(one.q, one.k_cache, one.weights, one.seq_lens, one.block_table)
     t1 = time.perf_counter() - t0
-    n = max(1, min(cpu.batch if max_queries is None else max_queries, int(budget_s / max(t1, 1e-4))))
+    n = max(1, min(w.batch if max_queries is None else max_queries, int(budget_s / max(t1, 1e-4))))
+    cpu, _ = w.compact(list(range(n)), "cpu")
     done, passes = 0, 0
     t0 = time.perf_counter()
     while True:
-        rt.indexer(cpu.q[:n], cpu.k_cache, cpu.weights[:n], cpu.seq_lens[:n], cpu.block_table[:n])
+        rt.indexer(cpu.q, cpu.k_cache, cpu.weights, cpu.seq_lens, cpu.block_table)
         done += n
         passes += 1
         dt = time.perf_counter() - t0
@@ -173,7 +177,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--config", type=int, default=2)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch-scale", type=float, default=1.0,
@@ -211,8 +215,14 @@ def main():
     pkg._lib.load()
 
     key_sharded = world > 1 and args.config in KEY_SHARDED_CONFIGS
-    seed = args.config if key_sharded else args.config + 1000 * rank
-    w = wl.config(args.config, device=dev, seed=seed, scale_batch=args.batch_scale)
+    # Every rank builds the same global workload (same seed); request-sharded
+    # ranks then keep their share of the rows, balanced by total length.
+    w = wl.config(args.config, device=dev, seed=args.config, scale_batch=args.batch_scale)
+    global_batch = w.batch
+    global_kbytes = w.kcache_bytes()
+    if world > 1 and not key_sharded:
+        sh = importlib.import_module(PKG_NAME + ".sharding")
+        w = w.rows(sh.request_shards(w.seq_lens, world)[rank])
     B = w.batch
     out = torch.empty((B, 2048), dtype=torch.int32, device=dev)
     flush = L2Flush(torch, dev)
@@ -238,10 +248,13 @@ def main():
 
         def call():
             return run_sharded(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table)
-    else:
+    elif B > 0:
         def call():
             pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, out)
             return pkg.last_launch_count()
+    else:  # a rank with no rows of the global batch (more ranks than rows)
+        def call():
+            return 0
 
     def barrier():
         if world > 1:
@@ -300,13 +313,13 @@ def main():
     # keep the bracketed kernel from overlapping its neighbours).
     pkg.set_kernel_timing(True)
     kms = []
-    for i in range(args.steps):
+    for i in range(args.steps if B > 0 else 0):
         flush()
         call()
         kms.append(pkg.last_kernel_ms())
     pkg.set_kernel_timing(False)
-    path = pkg.last_path()
-    kernel_ms = sum(kms) / len(kms)
+    path = pkg.last_path() if B > 0 else "idle"
+    kernel_ms = sum(kms) / len(kms) if kms else 0.0
 
     # ---------------- end-to-end region (host buffers) ----------------
     # A serving loop stages the step's small inputs (q, weights, seq_lens,
@@ -337,7 +350,7 @@ def main():
         d_in.copy_(h_in, non_blocking=True)
         if key_sharded:
             run_sharded(d_q, w.k_cache, d_w, d_sl, d_bt)
-        else:
+        elif B > 0:
             pkg.launch_topk_c(d_q, w.k_cache, d_w, d_sl, d_bt, out)
         h_out.copy_(out, non_blocking=True)
 
@@ -364,15 +377,22 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max, e2e_max, kms_max = float(t[0]), float(t[1]), float(t[2])
-    kbytes = w.kcache_bytes()
+    # Roofline of the slowest rank's dominant kernel: that rank's bytes.
+    kb = torch.tensor([float(kernel_ms), float(w.kcache_bytes())], dtype=torch.float64, device=dev)
+    if world > 1 and not key_sharded:
+        allk = [torch.zeros_like(kb) for _ in range(world)]
+        dist.all_gather(allk, kb)
+        kb = max(allk, key=lambda x: float(x[0]))
+    kbytes = int(kb[1])
     hbm, bf16, peak_src = peaks()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         qps, n, dt, threads, passes = cpu_reference_run(w, budget_s=10.0)
         cpu = {"value": qps, "unit": "queries/s", "cores": threads, "kind": "port",
-               "sample": f"{n} queries ({passes} passes over the first {n // passes} of {B} queries of {w.name}) "
-                         f"through the PyTorch CPU restatement (oracle/reference_torch.py), {dt:.2f} s"}
+               "sample": f"{n} queries ({passes} passes over the first {n // passes} of {B} queries of {w.name}, "
+                         f"their K pages copied to host memory) through the PyTorch CPU restatement "
+                         f"(oracle/reference_torch.py), {dt:.2f} s"}
 
     if rank == 0:
         kernel = "dsa::indexer_kernel<2> (partial, key range)" if key_sharded else DOMINANT.get(path, path)
@@ -381,7 +401,7 @@ def main():
             # K is L2-resident (one sequence): the contraction on the tensor
             # cores bounds the kernel. B200's dense fp8 rate is twice bf16.
             # Key-sharded: each rank's partial kernel scores 1/world of the keys.
-            flops = w.visible_keys() * FLOP_PER_KEY // (world if key_sharded else 1)
+            flops = (kbytes // 132) * FLOP_PER_KEY // (world if key_sharded else 1)
             achieved = flops / (kms_max * 1e-3) / 1e12
             roof = {"bound": "tensor", "achieved": achieved, "peak": 2 * bf16, "unit": "TFLOP/s",
                     "frac": achieved / (2 * bf16), "traffic": tr,
@@ -400,23 +420,24 @@ def main():
                      "kernel_timing": "CUDA events on the launching stream around the kernel, "
                                       "separate pass of the same steps"})
         line = {
-            "metric": METRIC, "value": B * (1 if key_sharded else world) / (ms_max * 1e-3), "unit": "queries/s",
+            "metric": METRIC, "value": global_batch / (ms_max * 1e-3), "unit": "queries/s",
             "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "strong" if key_sharded else "weak", "vs_baseline": None,
+            "scaling": "strong", "vs_baseline": None,
             "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": w.name + ("" if args.batch_scale == 1.0 else f" (batch x{args.batch_scale})"),
-                       "batch_per_gpu": B, "global_batch": B if key_sharded else B * world,
+                       "batch_per_gpu": B, "global_batch": global_batch,
                        "visible_keys_per_gpu": w.visible_keys() // (world if key_sharded else 1),
+                       "global_kcache_bytes": global_kbytes,
                        "max_pages": w.max_pages,
                        "pool_pages": w.num_pages,
                        "parallelism": (f"key-sharded x{world} (NCCL all-to-all of candidate lists, merge, all-gather "
                                        "of results)" if args.exchange == "alltoall" else
                                        f"key-sharded x{world} (NCCL all-gather of candidate lists + merge)")
                        if key_sharded
-                       else f"request-sharded x{world}",
+                       else f"request-sharded x{world} (rows split by total length, no collective)",
                        "l2": L2Flush.NOTE},
-            "e2e": {"value": B * (1 if key_sharded else world) / (e2e_max * 1e-3), "unit": "queries/s",
+            "e2e": {"value": global_batch / (e2e_max * 1e-3), "unit": "queries/s",
                     "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max,
                     "kcache": "resident in HBM (persistent serving state)"},
@@ -599,30 +620,51 @@ def sparse_attention_bench(args, rank, local):
 
 
 def reference_arm(args, rank, wl):
-    """The reference's CPU path (PyTorch restatement, all host threads) on the
-    same workload/metric; rank 0 only."""
+    """The reference's CPU path (the PyTorch restatement of its definition,
+    all host threads) on the same workload, metric and config; rank 0 only.
+    Each step is a bounded sample: the first n queries of the batch, n sized
+    so that the whole run takes about 150 s."""
     if rank != 0:
         return
     import torch
-    w = wl.config(args.config, device="cpu", seed=args.config)
-    total_budget = 150.0
-    per_step = total_budget / (args.steps + args.warmup)
-    times, ns = [], []
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import reference_torch as rt  # the reference arm's CPU implementation
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # The same seeded workload as the GPU arm (generated on the GPU when there
+    # is one: the generators are seeded per device); the sampled rows and the
+    # K pages they read are copied to host memory once.
+    gen_dev = "cuda" if torch.cuda.is_available() else "cpu"
+    w = wl.config(args.config, device=gen_dev, seed=args.config)
+    per_step = 150.0 / (args.steps + args.warmup)
+    one, _ = w.compact([0], "cpu")
+    t0 = time.perf_counter()
+    rt.indexer(one.q, one.k_cache, one.weights, one.seq_lens, one.block_table)
+    t1 = time.perf_counter() - t0
+    n = max(1, min(w.batch, int(per_step / max(t1, 1e-4))))
+    cpu, _ = w.compact(list(range(n)), "cpu")
+    global_batch = w.batch
+    del w
+    if gen_dev == "cuda":
+        torch.cuda.empty_cache()
+    times = []
     for i in range(args.warmup + args.steps):
-        qps, n, dt, threads, _ = cpu_reference_run(w, budget_s=per_step)
+        t0 = time.perf_counter()
+        rt.indexer(cpu.q, cpu.k_cache, cpu.weights, cpu.seq_lens, cpu.block_table)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
             times.append(dt)
-            ns.append(n)
-    value = sum(ns) / sum(times)
+    value = n * len(times) / sum(times)
     line = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": w.name, "batch_per_gpu": w.batch, "global_batch": w.batch},
+        "config": {"workload": cpu.name, "global_batch": global_batch},
         "cpu_baseline": {"value": value, "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": f"{ns[0]} queries per step (passes over up to {w.batch} queries), PyTorch "
-                                   "CPU restatement of the reference definition (oracle/reference_torch.py)"},
+                         "sample": f"the first {n} queries of the batch per step (their K pages in host memory), "
+                                   "PyTorch CPU restatement of the reference definition "
+                                   "(oracle/reference_torch.py)"},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

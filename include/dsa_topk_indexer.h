@@ -3,8 +3,20 @@
  *
  * All pointers are caller-owned, contiguous DEVICE buffers on the current
  * CUDA device; every call is asynchronous on `stream` (a cudaStream_t, NULL
- * for the legacy default stream). No entry point allocates device memory or
- * synchronises the stream. Return value: DSA_OK or a DSA_ERR_* code.
+ * for the legacy default stream) and never synchronises it. Return value:
+ * DSA_OK or a DSA_ERR_* code.
+ *
+ * Device memory the library allocates itself (never per call):
+ *   - dsa_topk_indexer_launch: a small per-(device, stream) workspace (the
+ *     longest-first row order and per-row flags, a few bytes per row) with
+ *     cudaMalloc, and a side stream with two events for its two-kernel
+ *     launch, on the first call on a stream whose batch needs them; grown
+ *     (never shrunk) when a later call needs more. Make the first call on a
+ *     stream outside stream capture.
+ *   - dsa_sparse_attention_launch: per-(device, stream) split buffers and
+ *     counters, allocated the first time a shape needs them (outside capture).
+ *   - dsa_topk_indexer_launch_noalloc allocates nothing (see below).
+ *   The other entry points allocate no device memory.
  *
  * Layouts (the reference operator dsa_topk_indexer_fp8_h64_d128_topk2048_ps64):
  *   q            [B, 64, 128]  FP8 e4m3 bytes
@@ -158,6 +170,18 @@ DSA_API int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe, co
                                         void* output, float* lse, int64_t num_tokens, int64_t num_indices,
                                         int64_t num_pages, void* stream);
 
+/* Test hook for the bounded-wait abort path (off by default). Every
+ * pipeline wait of the indexer kernels gives up after a time limit (2 s),
+ * raises DSA_STATUS_WAIT_TIMEOUT and ends the kernel early without a fault;
+ * this hook lets a test make that happen. While skip_tile >= 0, every CTA of
+ * later indexer calls (all entry points, all threads) never issues the loads
+ * of its local tile `skip_tile`, so the waits for it run out; wait_ns sets
+ * the limit of every wait (100 us .. 2 s; 0 restores the 2 s default).
+ * Outputs of such calls are meaningless. Call with (-1, 0) to turn it off.
+ * No counterpart in the reference, whose waits spin without a bound
+ * (solution/cuda/kernel.cu:107-120). */
+DSA_API int dsa_topk_indexer_set_test_fault(int skip_tile, int64_t wait_ns);
+
 /* Makes `device` the current CUDA device of the calling host thread for this
  * library (the entry points above run on the current device). Callers that
  * link their own CUDA runtime (PyTorch, TVM-FFI hosts) call it with the
@@ -176,14 +200,13 @@ DSA_API const char* dsa_topk_indexer_error_string(int code);
 DSA_API int dsa_topk_indexer_last_launch_count(void);
 
 /* Schedule the last successful top-K call on this host thread took:
- * "segmented" (plan, persistent stream kernel, cluster merge), "cluster"
- * (one cluster kernel, optionally after the longest-first plan) or
- * "cluster-split" (two concurrent cluster kernels). */
+ * "cluster" (one cluster kernel, optionally after the longest-first plan),
+ * "cluster-split" (two concurrent cluster kernels) or "noalloc" (the
+ * no-allocation entry point's cluster kernel). */
 DSA_API const char* dsa_topk_indexer_last_path(void);
 
 /* Per-kernel timing for profiling, off by default. While on, every call
- * records CUDA events on its stream around its dominant kernel (the stream
- * kernel of the segmented schedule, the cluster kernel or kernels otherwise)
+ * records CUDA events on its stream around its dominant kernel or kernels
  * and dsa_topk_indexer_kernel_ms waits for the last call on this host thread
  * and returns that kernel's device time in milliseconds. The events keep the
  * bracketed launch from overlapping its neighbours, so timed calls are not

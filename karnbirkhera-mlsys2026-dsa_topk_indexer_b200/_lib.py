@@ -25,6 +25,7 @@ SIGNATURES = [
     ("dsa_topk_indexer_partial", _I32, [_P, _P, _P, _P, _P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_merge", _I32, [_P, _P, _I64, _P, _P, _P, _I64, _I64, _P]),
     ("dsa_topk_indexer_launch_noalloc", _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
+    ("dsa_topk_indexer_set_test_fault", _I32, [_I32, _I64]),
     ("dsa_topk_indexer_set_device", _I32, [_I32]),
     ("dsa_topk_indexer_status", _I32, [_I32, ctypes.POINTER(ctypes.c_uint32), _I32]),
     ("dsa_topk_indexer_error_string", ctypes.c_char_p, [_I32]),

@@ -16,7 +16,6 @@
 
 #include "dsa_topk_indexer.h"
 #include "indexer_kernel.cuh"
-#include "segment_kernels.cuh"
 #include "cache_writer.cuh"
 #include "sparse_attention.cuh"
 
@@ -34,11 +33,17 @@ namespace dsa {
 constexpr int kMergeThreads = 256;
 constexpr int kMergeSmem = 3 * kTopK * 8;  // current result, next list, output
 
+// Positions outside [0, key_cap) (key_cap = max_pages * 64) are treated as
+// missing: they could not be translated through the block-table row, so a
+// list that holds one (e.g. lists paired with the wrong block-table rows)
+// flags DSA_STATUS_BAD_PAGE instead of reading past the row.
 __device__ __forceinline__ void load_list(const float* __restrict__ sc, const int32_t* __restrict__ ps,
-                                          uint64_t* dst) {
+                                          uint64_t* dst, int64_t key_cap) {
   for (int i = threadIdx.x; i < kTopK; i += kMergeThreads) {
     const int32_t pos = ps[i];
-    dst[i] = pos >= 0 ? pack_key(sc[i], static_cast<uint32_t>(pos)) : 0ull;
+    const bool ok = pos >= 0 && static_cast<int64_t>(pos) < key_cap;
+    if (pos >= 0 && !ok) atomicOr(&g_dsa_status, DSA_STATUS_BAD_PAGE);
+    dst[i] = ok ? pack_key(sc[i], static_cast<uint32_t>(pos)) : 0ull;
   }
 }
 
@@ -71,10 +76,11 @@ __global__ void __launch_bounds__(kMergeThreads)
   const int b = blockIdx.x;
   const int64_t row = static_cast<int64_t>(b) * kTopK;
   const int64_t part = static_cast<int64_t>(batch) * kTopK;
-  load_list(cand_scores + row, cand_pos + row, cur);
+  const int64_t key_cap = static_cast<int64_t>(max_pages) * kPage;
+  load_list(cand_scores + row, cand_pos + row, cur, key_cap);
 #pragma unroll 1
   for (int j = 1; j < nparts; ++j) {
-    load_list(cand_scores + j * part + row, cand_pos + j * part + row, nxt);
+    load_list(cand_scores + j * part + row, cand_pos + j * part + row, nxt, key_cap);
     __syncthreads();
     merge_top(cur, nxt, res);
     __syncthreads();
@@ -187,13 +193,6 @@ int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize, WriterGeom<false>::kSmem) != cudaSuccess ||
         cudaFuncSetAttribute(reinterpret_cast<const void*>(&sparse_attention_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, SaLayout::kBytes) != cudaSuccess)
-      return DSA_ERR_CUDA;
-    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_stream_kernel),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kS_SmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_merge_kernel),
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kM_SmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(reinterpret_cast<const void*>(&segment_merge_kernel),
-                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
       return DSA_ERR_CUDA;
     d.ready = true;
   }
@@ -426,148 +425,15 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   return DSA_OK;
 }
 
-int env_int(const char* name, int lo, int hi) {
-  if (const char* e = std::getenv(name)) {
-    const int v = std::atoi(e);
-    if (v >= lo && v <= hi) return v;
-  }
-  return 0;
-}
-
-size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
-
-// Segment-scheduled top-K (plan, persistent stream, cluster merge). Returns
-// DSA_ERR_CUDA-free "not taken" (1 in *taken = 0) when the workspace cannot be
-// had (first call on a stream inside capture) or the weights are not 16-byte
-// aligned; the caller then uses the cluster kernel.
-int launch_segmented(const void* q, const void* kcache, const float* w, const IndexerParams& prm, cudaStream_t stream,
-                     bool* taken) {
-  *taken = false;
-  if (!aligned16(w)) return DSA_OK;
-  int num_sms = 0;
-  int rc = prepare_device(&num_sms);
-  if (rc != DSA_OK) return rc;
-  const int64_t B = prm.batch;
-  const int64_t max_tiles = (static_cast<int64_t>(prm.max_pages) + 1) / 2;
-  // Segment length: about 16 segments per resident CTA for the longest
-  // possible rows (8..64 tiles), and at most 16384 workspace slots.
-  int64_t seg = (B * max_tiles + 16 * 2 * num_sms - 1) / (16 * 2 * num_sms);
-  seg = seg < 8 ? 8 : (seg > 64 ? 64 : seg);
-  const int64_t seg_floor = (B * max_tiles + 16383) / 16384;
-  if (seg < seg_floor) seg = seg_floor;
-  if (int v = env_int("DSA_TOPK_SEG", 2, 1 << 20)) seg = v;
-  seg += seg & 1;
-  const int64_t s_max = (max_tiles + seg - 1) / seg;
-  const int64_t slots = B * (s_max > 0 ? s_max : 1);
-  // Workspace carve-up.
-  size_t off = 0;
-  const size_t o_ctrl = off;
-  off = align256(off + 256);
-  const size_t o_order = off;
-  off = align256(off + 4 * B);
-  const size_t o_first = off;
-  off = align256(off + 4 * B);
-  const size_t o_cnt = off;
-  off = align256(off + 4 * B);
-  const size_t o_segs = off;
-  off = align256(off + 16 * slots);
-  const size_t o_n = off;
-  off = align256(off + 4 * slots);
-  const size_t o_cand = off;
-  off = align256(off + static_cast<size_t>(8) * kSegCap * slots);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(stream, off));
-  if (!ws) return DSA_OK;
-  CUtensorMap tk, ts, tq, tw;
-  rc = make_maps(q, kcache, B, prm.num_pages, &tk, &ts, &tq);
-  if (rc != DSA_OK) return rc;
-  {  // weights: {64 fp32, B}, box = one row
-    EncodeTiledFn enc = encode_fn();
-    std::memset(&tw, 0, sizeof(tw));
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHeads), static_cast<cuuint64_t>(B)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHeads * 4)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kHeads), 1};
-    const cuuint32_t estr[2] = {1, 1};
-    if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(w), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return DSA_ERR_CUDA;
-  }
-  SegPlan pl;
-  pl.ctrl = reinterpret_cast<uint32_t*>(ws + o_ctrl);
-  pl.order = reinterpret_cast<int32_t*>(ws + o_order);
-  pl.seg_first = reinterpret_cast<int32_t*>(ws + o_first);
-  pl.seg_cnt = reinterpret_cast<int32_t*>(ws + o_cnt);
-  pl.segs = reinterpret_cast<int4*>(ws + o_segs);
-  segment_plan_kernel<<<1, kSegPlanThreads, 0, stream>>>(prm.seq_lens, static_cast<int>(B), prm.max_pages,
-                                                         static_cast<int>(seg), pl);
-  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-  StreamParams sp;
-  sp.seq_lens = prm.seq_lens;
-  sp.block_table = prm.block_table;
-  sp.segs = pl.segs;
-  sp.ctrl = pl.ctrl;
-  sp.ws_cand = reinterpret_cast<uint64_t*>(ws + o_cand);
-  sp.ws_n = reinterpret_cast<uint32_t*>(ws + o_n);
-  sp.num_pages = prm.num_pages;
-  sp.max_pages = prm.max_pages;
-  sp.batch = prm.batch;
-  // The stream and merge kernels are programmatic dependents of the kernel
-  // before them: they launch and set up while it drains, and wait for its
-  // results with griddepcontrol.wait (DSA_TOPK_PDL=0 turns this off).
-  const char* pdl_env = std::getenv("DSA_TOPK_PDL");
-  const bool pdl = !(pdl_env && pdl_env[0] == '0');
-  {
-    cudaLaunchConfig_t scfg{};
-    scfg.gridDim = dim3(static_cast<unsigned>(2 * num_sms), 1, 1);
-    scfg.blockDim = dim3(kThreads, 1, 1);
-    scfg.dynamicSmemBytes = kS_SmemBytes;
-    scfg.stream = stream;
-    cudaLaunchAttribute sattr[1];
-    sattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    sattr[0].val.programmaticStreamSerializationAllowed = 1;
-    scfg.attrs = sattr;
-    scfg.numAttrs = pdl ? 1 : 0;
-    KernelTimer timer(stream);
-    if (cudaLaunchKernelEx(&scfg, segment_stream_kernel, tk, ts, tq, tw, sp) != cudaSuccess) return DSA_ERR_CUDA;
-    timer.stop();
-  }
-  // Merge: clusters of Gm CTAs per row, as many as fit in one wave of two
-  // CTAs per SM (a second wave would add a whole merge to the critical path).
-  int64_t gm = (2 * num_sms) / B;
-  if (gm > s_max) gm = s_max;
-  if (gm > 8) gm = 8;
-  if (gm < 1) gm = 1;
-  if (int v = env_int("DSA_TOPK_MERGE_CLUSTER", 1, 16)) gm = v;
-  MergeParams mp;
-  mp.order = pl.order;
-  mp.seg_first = pl.seg_first;
-  mp.seg_cnt = pl.seg_cnt;
-  mp.ws_cand = sp.ws_cand;
-  mp.ws_n = sp.ws_n;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(gm * B), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kM_SmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(gm);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;
-  if (cudaLaunchKernelEx(&cfg, segment_merge_kernel, mp, prm) != cudaSuccess) return DSA_ERR_CUDA;
-  t_last_launches = 3;
-  t_last_path = "segmented";
-  *taken = true;
-  return DSA_OK;
-}
+// Test hook of dsa_topk_indexer_set_test_fault (off by default).
+std::atomic<int> g_test_skip_tile{-1};
+std::atomic<uint64_t> g_test_wait_ns{ptx::kWaitTimeoutNs};
 
 IndexerParams base_params(const float* w, const int32_t* sl, const int32_t* bt, int64_t batch, int64_t max_pages,
                           int64_t num_pages) {
   IndexerParams p{};
+  p.skip_tile = g_test_skip_tile.load();
+  p.wait_ns = g_test_wait_ns.load();
   p.seq_lens = sl;
   p.block_table = bt;
   p.weights = w;
@@ -586,22 +452,12 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
                                        const int32_t* seq_lens, const int32_t* block_table, int32_t* topk_indices,
                                        int64_t batch, int64_t max_pages, int64_t num_pages, void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
   IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
-  // Path: the cluster kernel (one launch, or two concurrent ones, after the
-  // longest-first plan when the clusters take more than one wave). Measured
-  // on B200 it is at least as fast as the segment-scheduled kernels on every
-  // benchmark configuration (B=512 decode: 0.84 ms against 0.95 ms), so the
-  // segmented schedule (DSA_TOPK_PATH=segmented) is opt-in.
-  const char* path = std::getenv("DSA_TOPK_PATH");
-  if (path && std::strcmp(path, "segmented") == 0) {
-    bool taken = false;
-    rc = launch_segmented(q, k_cache, weights, p, static_cast<cudaStream_t>(stream), &taken);
-    if (rc != DSA_OK || taken) return rc;
-  }
   return launch_indexer<kModeTopK>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
 }
 
@@ -610,6 +466,7 @@ extern "C" int dsa_topk_indexer_scores(const void* q, const void* k_cache, const
                                        int64_t score_stride, int64_t batch, int64_t max_pages, int64_t num_pages,
                                        void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!scores || score_stride < max_pages * kPage) return DSA_ERR_INVALID_ARG;
@@ -633,6 +490,7 @@ extern "C" int dsa_topk_indexer_partial(const void* q, const void* k_cache, cons
                                         int64_t key_end, float* cand_scores, int32_t* cand_pos, int64_t batch,
                                         int64_t max_pages, int64_t num_pages, void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!cand_scores || !cand_pos || key_begin < 0 || key_end < key_begin) return DSA_ERR_INVALID_ARG;
@@ -650,6 +508,7 @@ extern "C" int dsa_topk_indexer_merge(const float* cand_scores, const int32_t* c
                                       const int32_t* seq_lens, const int32_t* block_table, int32_t* topk_indices,
                                       int64_t batch, int64_t max_pages, void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   if (batch < 0 || nparts < 1 || max_pages < 1 || max_pages > INT32_MAX / kPage || batch > INT32_MAX)
     return DSA_ERR_INVALID_ARG;
   if (batch == 0) return DSA_OK;
@@ -697,6 +556,7 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
                                                int32_t* topk_indices, int64_t batch, int64_t max_pages,
                                                int64_t num_pages, void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
@@ -739,8 +599,20 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  KernelTimer timer(st);
   if (cudaLaunchKernelEx(&cfg, indexer_kernel<kModeTopK>, tk, ts, tq, p) != cudaSuccess) return DSA_ERR_CUDA;
+  timer.stop();
   t_last_launches = launches;
+  t_last_path = "noalloc";
+  return DSA_OK;
+}
+
+extern "C" int dsa_topk_indexer_set_test_fault(int skip_tile, int64_t wait_ns) {
+  if (skip_tile < -1 || wait_ns < 0 || wait_ns > static_cast<int64_t>(ptx::kWaitTimeoutNs) ||
+      (wait_ns > 0 && wait_ns < 100000))
+    return DSA_ERR_INVALID_ARG;
+  g_test_skip_tile.store(skip_tile);
+  g_test_wait_ns.store(wait_ns == 0 ? ptx::kWaitTimeoutNs : static_cast<uint64_t>(wait_ns));
   return DSA_OK;
 }
 
@@ -804,6 +676,7 @@ extern "C" int dsa_topk_indexer_kernel_ms(float* ms) {
 extern "C" int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* slots, void* k_cache,
                                      int64_t num_tokens, int64_t num_pages, void* stream) {
   t_last_launches = 0;
+  t_timed = false;
   if (num_tokens < 0 || num_pages < 1) return DSA_ERR_INVALID_ARG;
   if (num_tokens == 0) return DSA_OK;
   if (!k || !slots || !k_cache || (k_dtype != DSA_DTYPE_BF16 && k_dtype != DSA_DTYPE_F32))
@@ -923,6 +796,7 @@ extern "C" int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe,
                                            int64_t num_pages, void* stream) {
   using namespace dsa;
   t_last_launches = 0;
+  t_timed = false;
   if (num_tokens < 0 || num_indices < 0 || num_pages < 1) return DSA_ERR_INVALID_ARG;
   if (num_tokens == 0) return DSA_OK;
   if (!q_nope || !q_pe || !ckv_cache || !kpe_cache || !output || !lse || (num_indices > 0 && !sparse_indices))

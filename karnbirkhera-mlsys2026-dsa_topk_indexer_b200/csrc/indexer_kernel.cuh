@@ -116,6 +116,11 @@ struct IndexerParams {
   // rank is order_base + cluster index, computed in the kernel (small
   // batches: saves the plan launch).
   int32_t order_base = -1;
+  // Test hook (off: -1): every CTA's producer skips the loads of its local
+  // tile `skip_tile`, so the waits for that tile run out after wait_ns and
+  // the kernel takes its abort path.
+  int32_t skip_tile = -1;
+  uint64_t wait_ns = ptx::kWaitTimeoutNs;  // bound of every pipeline wait
 };
 
 constexpr int kInKernelOrderMax = 256;  // rows ranked in-kernel at most
@@ -186,9 +191,7 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
 // Cluster-wide exact selection of the best 2048 of all candidates held by the
 // G CTAs of this cluster (n in this CTA's cand buffer), survivors gathered in
 // CTA 0's shared memory, ordered and emitted for row b. Called by all
-// kThreads threads of every CTA of the cluster, with the K ring free. Shared
-// by the streaming cluster kernel and the segment merge kernel, which use the
-// same shared-memory map.
+// kThreads threads of every CTA of the cluster, with the K ring free.
 // Shared-memory offsets cluster_select_emit works with. `Final` receives the
 // survivors of every CTA (written remotely) and must not overlap `Cand`;
 // the ordering scratch (`RankTmp`, `RankCnt`) is only touched after the last
@@ -446,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = misc_nv[kMiscTmem];
 
   int issued = 0;      // producer: tiles whose loads were issued
+  int skipped = -1;    // producer: the tile the test hook left unloaded
   int mma_issued = 0;  // MMA warp: tiles whose MMAs were issued
   bool aborted = false;
 
@@ -468,10 +472,16 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool has_b = (pg_first + 2 * i + 1) < pg_end;
       const int s = i % kStages;
       const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-      const bool ok = ptx::mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+      const bool ok = ptx::mbar_wait(bar_empty + 8 * s, ph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
+                                     p.wait_ns);
       if (__any_sync(0xFFFFFFFFu, !ok)) {
         aborted = true;
         break;
+      }
+      if (i == p.skip_tile) {  // test hook: this tile's loads are never issued
+        skipped = i;
+        issued = i + 1;
+        continue;
       }
       if (lane == 0) {
         if (static_cast<uint64_t>(static_cast<uint32_t>(pa)) >= static_cast<uint64_t>(p.num_pages) ||
@@ -496,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // ===================== MMA issuer =====================
     constexpr uint32_t idesc = ptx::idesc_e4m3_f32(kTileKeys, kHeads);
     bool ok = true;
-    if (my_tiles > 0) ok = ptx::mbar_wait(bar_q, 0u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+    if (my_tiles > 0) ok = ptx::mbar_wait(bar_q, 0u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
     const uint64_t qdesc = ptx::sw128_kmajor_desc(base_addr + kOffQ);
 #pragma unroll 1
@@ -505,8 +515,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
       const int buf = i % kTmemBufs;
       const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
-      ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT) &&
-           ptx::mbar_wait(bar_tempty + 8 * buf, bph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+      ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns) &&
+           ptx::mbar_wait(bar_tempty + 8 * buf, bph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
+                          p.wait_ns);
       if (__any_sync(0xFFFFFFFFu, !ok)) {
         aborted = true;
         break;
@@ -554,58 +565,63 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       pm = 0u;
     };
+    // A warp whose wait gave up (`aborted`, warp-uniform) stops touching the
+    // pipeline but keeps walking the same tile schedule with no keys, so it
+    // still meets the other group at every check barrier below: leaving the
+    // loop early would strand the other group at a named barrier.
 #pragma unroll 1
     for (int i = grp; i < my_tiles; i += 2) {
       const int s = i % kStages;
       const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
-      bool ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
-      if (__any_sync(0xFFFFFFFFu, !ok)) {
-        aborted = true;
-        break;
+      float score = 0.f;
+      if (!aborted) {
+        const bool ok =
+            ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
+        if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
       }
-      // The scale is read with a generic-proxy load, and the producer's next
-      // TMA into this stage writes through the async proxy as soon as the MMA
-      // commit and this group's four warps have arrived. Without the proxy
-      // fence that write-after-read is unordered: on L2-resident pages the
-      // refill landed first and the key was scaled by the scale of the tile
-      // four steps ahead.
-      const float scale = ptx::lds_f32_ordered(base_addr + kOffScale + 4u * (s * kTileKeys + row));
-      ptx::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
       const int buf = i % kTmemBufs;
-      const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
-      ok = ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
-      if (__any_sync(0xFFFFFFFFu, !ok)) {
-        aborted = true;
-        break;
+      if (!aborted) {
+        // The scale is read with a generic-proxy load, and the producer's next
+        // TMA into this stage writes through the async proxy as soon as the MMA
+        // commit and this group's four warps have arrived. Without the proxy
+        // fence that write-after-read is unordered: on L2-resident pages the
+        // refill landed first and the key was scaled by the scale of the tile
+        // four steps ahead.
+        const float scale = ptx::lds_f32_ordered(base_addr + kOffScale + 4u * (s * kTileKeys + row));
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
+        const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
+        const bool ok =
+            ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
+        if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
+        if (!aborted) {
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+          ptx::tc_fence_after();
+          float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          {
+            uint32_t acc[32];
+            const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(buf * kHeads);
+            ptx::tmem_ld_32x32b_x32_sync(ta, acc);
+            if (scale >= 0.f)
+              head_reduce_half<false>(acc, s_w, 0, sums);
+            else
+              head_reduce_half<true>(acc, s_w, 0, sums);
+            ptx::tmem_ld_32x32b_x32_sync(ta + 32u, acc);
+            if (scale >= 0.f)
+              head_reduce_half<false>(acc, s_w, 32, sums);
+            else
+              head_reduce_half<true>(acc, s_w, 32, sums);
+          }
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
+          score = (((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]))) *
+                  fabsf(scale);
+        }
       }
-      __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
-      ptx::tc_fence_after();
-      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      {
-        uint32_t acc[32];
-        const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(buf * kHeads);
-        ptx::tmem_ld_32x32b_x32_sync(ta, acc);
-        if (scale >= 0.f)
-          head_reduce_half<false>(acc, s_w, 0, sums);
-        else
-          head_reduce_half<true>(acc, s_w, 0, sums);
-        ptx::tmem_ld_32x32b_x32_sync(ta + 32u, acc);
-        if (scale >= 0.f)
-          head_reduce_half<false>(acc, s_w, 32, sums);
-        else
-          head_reduce_half<true>(acc, s_w, 32, sums);
-      }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
-
-      const float score =
-          (((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]))) *
-          fabsf(scale);
       const int64_t pos = static_cast<int64_t>(pg_first + 2 * i) * kPage + row;
-      const bool valid = pos >= key_lo && pos < key_hi;
+      const bool valid = !aborted && pos >= key_lo && pos < key_hi;
       if (kMode == kModeScores) {
         if (valid) p.scores[static_cast<int64_t>(b) * p.score_stride + pos] = score;
       } else {
@@ -676,13 +692,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     volatile uint32_t no_abort = 0u;
     if (warp == 0 && lane == 0) {
       for (int i = (issued > kStages ? issued - kStages : 0); i < issued; ++i)
-        ptx::mbar_wait(bar_full + 8 * (i % kStages), static_cast<uint32_t>(i / kStages) & 1u, &no_abort,
-                       &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+        if (i != skipped)
+          ptx::mbar_wait(bar_full + 8 * (i % kStages), static_cast<uint32_t>(i / kStages) & 1u, &no_abort,
+                         &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     }
     if (warp == 1 && lane == 0 && mma_issued > 0) {
       const int last = mma_issued - 1;
       ptx::mbar_wait(bar_tfull + 8 * (last % kTmemBufs), static_cast<uint32_t>(last / kTmemBufs) & 1u,
-                     &no_abort, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT);
+                     &no_abort, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     }
     __syncthreads();
   }

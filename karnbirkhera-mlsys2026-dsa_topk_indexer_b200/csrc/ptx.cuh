@@ -56,11 +56,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with the given parity to complete. Returns false on
-// timeout or when *abort is already set; on timeout it raises *abort and ORs
-// `timeout_bit` into *status.
+// Waits for the phase with the given parity to complete. Returns false after
+// `limit_ns` of wall time or when *abort is already set; on timeout it raises
+// *abort and ORs `timeout_bit` into *status.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile uint32_t* abort,
-                                          unsigned int* status, unsigned int timeout_bit) {
+                                          unsigned int* status, unsigned int timeout_bit,
+                                          uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
@@ -68,7 +69,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort = 1u;
       atomicOr(status, timeout_bit);
       return false;

@@ -54,6 +54,41 @@ class Workload:
         return Workload(self.name, self.q.to(device), self.k_cache.to(device), self.weights.to(device),
                         self.seq_lens.to(device), self.block_table.to(device), dict(self.meta))
 
+    def rows(self, idx):
+        """The requests `idx` (in that order) over the same K cache."""
+        idx = torch.as_tensor(idx, dtype=torch.int64, device=self.q.device)
+        return Workload(self.name, self.q[idx].contiguous(), self.k_cache, self.weights[idx].contiguous(),
+                        self.seq_lens[idx].contiguous(), self.block_table[idx].contiguous(), dict(self.meta))
+
+    def compact(self, idx=None, device="cpu"):
+        """The requests `idx` (default: all) with a K cache holding only the
+        pages they can read, renumbered, on `device`. Returns (workload,
+        used) where `used[j]` is the original id of new page j, so a slot s
+        of the compact cache is slot used[s // 64] * 64 + s % 64 of this one.
+        Page ids outside the pool (never valid) are kept as they are."""
+        import numpy as np
+        w = self if idx is None else self.rows(idx)
+        sl = w.seq_lens.clamp(min=0, max=w.max_pages * PAGE).to(torch.int64).cpu()
+        bt = w.block_table.cpu().to(torch.int64)
+        npg = (sl + PAGE - 1) // PAGE
+        mask = torch.arange(bt.shape[1]).view(1, -1) < npg.view(-1, 1)
+        ids = bt[mask]
+        ok = (ids >= 0) & (ids < self.num_pages)
+        used = torch.unique(ids[ok])
+        remap = torch.full((self.num_pages,), -1, dtype=torch.int64)
+        remap[used] = torch.arange(used.numel())
+        bt_new = bt.clone()
+        sel = mask & (bt >= 0) & (bt < self.num_pages)
+        bt_new[sel] = remap[bt[sel]]
+        bt_new[~mask] = 0
+        bad = mask & ~sel  # out-of-pool ids stay out of the (smaller) pool
+        bt_new[bad] = used.numel() + (bt[bad] - bt[bad].clamp(0, self.num_pages - 1)).abs()
+        kc = self.k_cache[used.to(self.k_cache.device)].to(device) if used.numel() else \
+            torch.zeros((1, PAGE, 1, DIM + 4), dtype=torch.uint8, device=device)
+        out = Workload(w.name, w.q.to(device), kc, w.weights.to(device), w.seq_lens.to(device),
+                       bt_new.to(torch.int32).to(device), dict(w.meta))
+        return out, np.asarray(used.numpy())
+
 
 def e4m3(x):
     return x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)

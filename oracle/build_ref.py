@@ -9,8 +9,12 @@ golden vectors against outputs of the reference itself, run on a B200, and
 sources are not copied into this repository; only the build output is written
 (into oracle/_ref/, which git ignores but which travels to the GPU machine).
 
-Run here (needs the reference checkout and nvcc, no GPU):
+Run on the development machine (needs the reference checkout and nvcc, no
+GPU):
     python oracle/build_ref.py [/path/to/reference]
+The checkout is found from the argument, else the DSA_REFERENCE_ROOT
+environment variable, else a directory named "reference" beside this
+repository.
 """
 import glob
 import importlib.util
@@ -22,8 +26,22 @@ OUT = os.path.join(HERE, "_ref")
 NAME = "dsa_ref_kernel"
 
 
-def build(ref_root="/root/reference"):
-    src = os.path.join(ref_root, "solution", "cuda", "kernel.cu")
+def default_root():
+    """The reference checkout: $DSA_REFERENCE_ROOT, else ../reference next to
+    this repository."""
+    env = os.environ.get("DSA_REFERENCE_ROOT")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
+def source(ref_root=None):
+    """Path of the reference's kernel.cu (it may not exist)."""
+    return os.path.join(ref_root or default_root(), "solution", "cuda", "kernel.cu")
+
+
+def build(ref_root=None):
+    src = source(ref_root)
     if not os.path.exists(src):
         raise FileNotFoundError(src)
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"  # as the reference's binding.py:13 sets it

@@ -62,6 +62,19 @@ def test_noalloc_matches_regular_entry_two_calls():
         fails = check_all(got_np, ref_o, rows, w_cpu.seq_lens.numpy(), w_cpu.block_table.numpy(), w_cpu.num_pages)
         assert not fails, fails[:3]
     assert pkg.device_status(0) == 0
+    # The no-allocation call reports its own schedule and, with timing on,
+    # its own kernel time (not an earlier call's).
+    w = cases[0].to("cuda")
+    got = torch.empty((w.batch, 2048), dtype=torch.int32, device="cuda")
+    pkg.set_kernel_timing(True)
+    try:
+        assert _call(lib, "dsa_topk_indexer_launch", w, got) == 0
+        assert _call(lib, "dsa_topk_indexer_launch_noalloc", w, got) == 0
+        assert pkg.last_path() == "noalloc"
+        assert pkg.last_kernel_ms() > 0.0
+    finally:
+        pkg.set_kernel_timing(False)
+    torch.cuda.synchronize()
 
 
 def test_noalloc_rejects_batch_above_capacity():
