@@ -49,7 +49,10 @@ def traffic_per_launch(config, kernel):
     return json.load(open(p)).get(f"cfg{config}:{kernel}")
 
 
-DOMINANT = {"cluster": "dsa::indexer_kernel<0>", "cluster-split": "dsa::indexer_kernel<0>"}
+DOMINANT = {"cluster": "dsa::indexer_kernel<0>", "cluster-split": "dsa::indexer_kernel<0>",
+            "prefill+cluster": "dsa::prefill_kernel<0> + dsa::indexer_kernel<0>"}
+DOMINANT_PARTIAL = {"cluster": "dsa::indexer_kernel<2>", "cluster-split": "dsa::indexer_kernel<2>",
+                    "prefill+cluster": "dsa::prefill_kernel<2> + dsa::indexer_kernel<2>"}
 PREFILL_CONFIGS = (3, 4)
 # Configs whose single sequence is split along the key axis across ranks
 # (every rank holds the same inputs; partial top-K, NCCL all-gather, merge).
@@ -235,6 +238,9 @@ def main():
         def pfn(*a):
             r = pkg.indexer_partial(*a)
             counts["p"] = pkg.last_launch_count()
+            counts["path"] = pkg.last_path()
+            if counts.get("timing"):  # the merge call after this one resets the kernel timer
+                counts["kms"] = pkg.last_kernel_ms()
             return r
 
         def mfn(*a):
@@ -313,12 +319,16 @@ def main():
     # keep the bracketed kernel from overlapping its neighbours).
     pkg.set_kernel_timing(True)
     kms = []
+    if key_sharded:
+        counts["timing"] = True
     for i in range(args.steps if B > 0 else 0):
         flush()
         call()
-        kms.append(pkg.last_kernel_ms())
+        kms.append(counts["kms"] if key_sharded else pkg.last_kernel_ms())
     pkg.set_kernel_timing(False)
-    path = pkg.last_path() if B > 0 else "idle"
+    if key_sharded:
+        counts["timing"] = False
+    path = (counts["path"] if key_sharded else pkg.last_path()) if B > 0 else "idle"
     kernel_ms = sum(kms) / len(kms) if kms else 0.0
 
     # ---------------- end-to-end region (host buffers) ----------------
@@ -395,7 +405,7 @@ def main():
                          f"(oracle/reference_torch.py), {dt:.2f} s"}
 
     if rank == 0:
-        kernel = "dsa::indexer_kernel<2> (partial, key range)" if key_sharded else DOMINANT.get(path, path)
+        kernel = (DOMINANT_PARTIAL.get(path, path) + " (partial, key range)") if key_sharded else DOMINANT.get(path, path)
         tr = traffic_per_launch(args.config, kernel)
         if args.config in PREFILL_CONFIGS:
             # K is L2-resident (one sequence): the contraction on the tensor

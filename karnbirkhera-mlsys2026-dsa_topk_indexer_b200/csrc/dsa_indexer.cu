@@ -16,6 +16,7 @@
 
 #include "dsa_topk_indexer.h"
 #include "indexer_kernel.cuh"
+#include "prefill_kernel.cuh"
 #include "cache_writer.cuh"
 #include "sparse_attention.cuh"
 
@@ -185,6 +186,11 @@ int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
           cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
         return DSA_ERR_CUDA;
     }
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&prefill_kernel<kModeTopK>),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(reinterpret_cast<const void*>(&prefill_kernel<kModePartial>),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes) != cudaSuccess)
+      return DSA_ERR_CUDA;
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&merge_kernel),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmem) != cudaSuccess ||
         cudaFuncSetAttribute(reinterpret_cast<const void*>(&cache_write_kernel<true>),
@@ -343,6 +349,13 @@ int check_common(const void* q, const void* kcache, const float* w, const int32_
   return DSA_OK;
 }
 
+// Batches of at least this many rows first go through the shared-sequence
+// kernel (prefill_kernel), which serves every group of four consecutive rows
+// that read the same pages (causal prefill rows of one sequence) and leaves
+// the others to the per-row kernel. Smaller batches skip it: for them its
+// extra launch would cost more than it can save.
+constexpr int64_t kPrefillMinRows = 256;
+
 template <int kMode>
 int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, int64_t span_pages,
                    cudaStream_t stream) {
@@ -370,6 +383,38 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
   };
+
+  // Shared-sequence stage: plan (row order + group order), then the prefill
+  // kernel over the groups, longest first; the per-row kernel below skips
+  // the rows it served. DSA_TOPK_PREFILL=0 turns the stage off.
+  if constexpr (kMode != kModeScores) {
+    const char* env = std::getenv("DSA_TOPK_PREFILL");
+    const int64_t B = prm.batch;
+    const int64_t ngroups = (B + kGroupRows - 1) / kGroupRows;
+    uint8_t* ws = (B < kPrefillMinRows || (env && env[0] == '0'))
+                      ? nullptr
+                      : static_cast<uint8_t*>(workspace(stream, static_cast<size_t>(8 * B + 4 * ngroups)));
+    if (ws) {
+      int32_t* order = reinterpret_cast<int32_t*>(ws);
+      int32_t* handled = order + B;
+      int32_t* group_order = handled + B;
+      lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order, group_order);
+      if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+      PrefillParams pp{group_order, handled};
+      KernelTimer timer(stream);
+      prefill_kernel<kMode><<<static_cast<unsigned>(ngroups), kPThreads, kPSmemBytes, stream>>>(tk, ts, tq, prm, pp);
+      if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+      params.order = order;
+      params.order_base = -1;
+      params.handled = handled;
+      if ((rc = launch(params, prm.batch, G, stream)) != DSA_OK) return rc;
+      timer.stop();
+      t_last_launches = 3;
+      t_last_path = "prefill+cluster";
+      return DSA_OK;
+    }
+  }
+
   // More clusters than fit at once: serve the longest rows first so that no
   // long row starts in the last wave. Small batches rank their rows inside
   // the kernel (no plan launch); larger ones get a one-CTA plan kernel.
@@ -381,7 +426,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     } else {
       order = static_cast<int32_t*>(workspace(stream, static_cast<size_t>(prm.batch) * sizeof(int32_t)));
       if (order) {
-        lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order);
+        lpt_order_kernel<<<1, kPlanThreads, 0, stream>>>(prm.seq_lens, prm.batch, prm.max_pages, order, nullptr);
         if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
         params.order = order;
         launches = 2;
@@ -581,7 +626,7 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
     } else {
       // The plan kernel writes all `batch` entries the indexer reads.
       lpt_order_kernel<<<1, kPlanThreads, 0, st>>>(seq_lens, static_cast<int>(batch), static_cast<int>(max_pages),
-                                                   order);
+                                                   order, nullptr);
       if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
       p.order = order;
       launches = 2;

@@ -121,6 +121,9 @@ struct IndexerParams {
   // the kernel takes its abort path.
   int32_t skip_tile = -1;
   uint64_t wait_ns = ptx::kWaitTimeoutNs;  // bound of every pipeline wait
+  // [B] or null: rows whose entry is nonzero were served by the
+  // shared-sequence kernel launched before this one and are skipped.
+  const int32_t* handled = nullptr;
 };
 
 constexpr int kInKernelOrderMax = 256;  // rows ranked in-kernel at most
@@ -225,7 +228,7 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
         mm[1] = 0ull;
       }
       __syncthreads();
-      group_minmax<kThreads, 0>(cand, n, mm, tid);
+      group_minmax<kThreads>(cand, n, mm, tid, 0);
       if (tid >= 256) return;
       RankScratch sc;
       sc.tmp = reinterpret_cast<uint64_t*>(smem + L::kSoloTmp);
@@ -237,10 +240,10 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
       const int64_t o = static_cast<int64_t>(b) * kTopK;
       if (kMode == kModeTopK) {
         EmitSlots e{p.out + o, bt_row};
-        block_rank_emit<kBarLow, kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e);
+        block_rank_emit<kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e, tid, kBarLow);
       } else {
         EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
-        block_rank_emit<kBarLow, kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e);
+        block_rank_emit<kSoloCap / 256>(cand, n, mm[0], mm[1], sc, e, tid, kBarLow);
       }
       return;
     }
@@ -253,7 +256,7 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
     mm[1] = 0ull;
   }
   __syncthreads();
-  group_minmax<kThreads, 0>(cand, n, mm, tid);
+  group_minmax<kThreads>(cand, n, mm, tid, 0);
   if (tid == 0) {
     misc_nv[kMiscPub] = n;
     pub_mm[0] = mm[0];
@@ -355,10 +358,10 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   const int64_t o = static_cast<int64_t>(b) * kTopK;
   if (kMode == kModeTopK) {
     EmitSlots e{p.out + o, bt_row};
-    block_rank_emit<kBarLow, 8>(fin, nsel, kmin, kmax, sc, e);
+    block_rank_emit<8>(fin, nsel, kmin, kmax, sc, e, tid, kBarLow);
   } else {
     EmitCandidates e{p.cand_scores + o, p.cand_pos + o};
-    block_rank_emit<kBarLow, 8>(fin, nsel, kmin, kmax, sc, e);
+    block_rank_emit<8>(fin, nsel, kmin, kmax, sc, e, tid, kBarLow);
   }
 }
 
@@ -393,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     ? row_of_rank(p, p.order_base + static_cast<int>(blockIdx.x / G),
                                   reinterpret_cast<int32_t*>(smem + kOffCand), misc_nv + kMiscSel)
                     : (p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G));
+  if (p.handled && p.handled[b]) return;  // uniform over the cluster, before any barrier or TMEM use
 
   // ---- request geometry (identical in every thread) ----
   int64_t len = p.seq_lens[b];
@@ -662,10 +666,10 @@ __global__ void __launch_bounds__(kThreads, 2)
                 mm[1] = 0ull;
               }
               ptx::named_bar(kBarEpi, kEpiThreads);
-              group_minmax<kEpiThreads, kBarEpi>(cand, n, mm, et);
-              const uint64_t T = group_select<kEpiThreads, kBarEpi>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et);
-              group_compact<kEpiThreads, kBarEpi, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount,
-                                                                     misc_nv + kMiscWsum, et);
+              group_minmax<kEpiThreads>(cand, n, mm, et, kBarEpi);
+              const uint64_t T = group_select<kEpiThreads>(cand, n, kTopK, mm, hist, misc_nv + kMiscSel, et, kBarEpi);
+              group_compact<kEpiThreads, kCap / kEpiThreads>(cand, n, T, misc_nv + kMiscCount, misc_nv + kMiscWsum,
+                                                            et, kBarEpi);
               thr = T;
               n_base = misc[kMiscCount];
             }
@@ -716,28 +720,25 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // Longest-first request order for the indexer's clusters (one CTA of 1024
 // threads): counting sort of the rows' tile counts, descending. Rows whose
-// counts fall in the same bucket keep no particular order.
+// counts fall in the same bucket keep no particular order. With group_order
+// non-null it also orders the groups of kGroupRows consecutive rows (the
+// shared-sequence kernel's work items) by their longest row, the same way.
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanBuckets = 4096;
+constexpr int kGroupRows = 4;
 
-__global__ void __launch_bounds__(kPlanThreads, 1)
-    lpt_order_kernel(const int32_t* __restrict__ seq_lens, int batch, int max_pages, int32_t* __restrict__ order) {
-  __shared__ uint32_t cnt[kPlanBuckets];
-  __shared__ uint32_t start[kPlanBuckets];
-  __shared__ uint32_t wsum[kPlanThreads / 32];
+// Descending counting sort of n items by tile count tiles(i) in [0, max_tiles]
+// into out[0..n). All kPlanThreads threads; cnt/start hold kPlanBuckets words.
+template <class Tiles>
+__device__ void plan_sort_desc(int n, int max_tiles, Tiles tiles, int32_t* __restrict__ out, uint32_t* cnt,
+                               uint32_t* start, uint32_t* wsum) {
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
-  const int max_tiles = (max_pages + 1) / 2;
   int shift = 0;
   while ((max_tiles >> shift) >= kPlanBuckets) ++shift;
   for (int i = t; i < kPlanBuckets; i += kPlanThreads) cnt[i] = 0u;
   __syncthreads();
-  auto bucket = [&](int b) {
-    int64_t len = seq_lens[b];
-    len = len < 0 ? 0 : (len > static_cast<int64_t>(max_pages) * kPage ? static_cast<int64_t>(max_pages) * kPage : len);
-    const int tiles = static_cast<int>((len + 2 * kPage - 1) / (2 * kPage));
-    return (kPlanBuckets - 1) - (tiles >> shift);  // descending: longest rows in bucket 0
-  };
-  for (int b = t; b < batch; b += kPlanThreads) atomicAdd(&cnt[bucket(b)], 1u);
+  auto bucket = [&](int i) { return (kPlanBuckets - 1) - (tiles(i) >> shift); };  // longest in bucket 0
+  for (int i = t; i < n; i += kPlanThreads) atomicAdd(&cnt[bucket(i)], 1u);
   __syncthreads();
   // exclusive scan over the 4096 buckets: thread t owns buckets 4t..4t+3
   uint32_t c[4], tot = 0;
@@ -762,7 +763,34 @@ __global__ void __launch_bounds__(kPlanThreads, 1)
     base += c[j];
   }
   __syncthreads();
-  for (int b = t; b < batch; b += kPlanThreads) order[atomicAdd(&start[bucket(b)], 1u)] = b;
+  for (int i = t; i < n; i += kPlanThreads) out[atomicAdd(&start[bucket(i)], 1u)] = i;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kPlanThreads, 1)
+    lpt_order_kernel(const int32_t* __restrict__ seq_lens, int batch, int max_pages, int32_t* __restrict__ order,
+                     int32_t* __restrict__ group_order) {
+  __shared__ uint32_t cnt[kPlanBuckets];
+  __shared__ uint32_t start[kPlanBuckets];
+  __shared__ uint32_t wsum[kPlanThreads / 32];
+  const int max_tiles = (max_pages + 1) / 2;
+  auto row_tiles = [&](int b) {
+    int64_t len = seq_lens[b];
+    len = len < 0 ? 0 : (len > static_cast<int64_t>(max_pages) * kPage ? static_cast<int64_t>(max_pages) * kPage : len);
+    return static_cast<int>((len + 2 * kPage - 1) / (2 * kPage));
+  };
+  plan_sort_desc(batch, max_tiles, row_tiles, order, cnt, start, wsum);
+  if (group_order) {
+    auto group_tiles = [&](int g) {
+      int m = 0;
+      for (int r = g * kGroupRows; r < (g + 1) * kGroupRows && r < batch; ++r) {
+        const int x = row_tiles(r);
+        m = x > m ? x : m;
+      }
+      return m;
+    };
+    plan_sort_desc((batch + kGroupRows - 1) / kGroupRows, max_tiles, group_tiles, group_order, cnt, start, wsum);
+  }
 }
 
 }  // namespace dsa

@@ -35,14 +35,14 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
   return m;
 }
 
-// Group barrier: BAR == 0 is __syncthreads(), otherwise a named barrier over
-// the NT threads of the group.
-template <int NT, int BAR>
-__device__ __forceinline__ void group_sync() {
-  if (BAR == 0)
+// Group barrier: bar == 0 is __syncthreads(), otherwise named barrier `bar`
+// over the NT threads of the group (a warp-aligned set of warps).
+template <int NT>
+__device__ __forceinline__ void group_sync(uint32_t bar) {
+  if (bar == 0)
     __syncthreads();
   else
-    ptx::named_bar(BAR, NT);
+    ptx::named_bar(bar, NT);
 }
 
 // Radix-select state: the top `top` bits of the sought key are known and
@@ -106,8 +106,8 @@ __device__ __forceinline__ void find_digit_warp(const uint32_t* hist, uint32_t k
 
 // Min and max of cand[0..n) over a group (results in mm[0], mm[1]; mm must be
 // preset to {~0, 0} before the group barrier that precedes the call).
-template <int NT, int BAR>
-__device__ void group_minmax(const uint64_t* cand, uint32_t n, unsigned long long* mm, int gt) {
+template <int NT>
+__device__ void group_minmax(const uint64_t* cand, uint32_t n, unsigned long long* mm, int gt, uint32_t bar) {
   unsigned long long lo = ~0ull, hi = 0ull;
   for (uint32_t i = gt; i < n; i += NT) {
     const unsigned long long k = cand[i];
@@ -125,7 +125,7 @@ __device__ void group_minmax(const uint64_t* cand, uint32_t n, unsigned long lon
     atomicMin(&mm[0], lo);
     atomicMax(&mm[1], hi);
   }
-  group_sync<NT, BAR>();
+  group_sync<NT>(bar);
 }
 
 // One histogram pass of the radix select over cand[0..n) (plain per-lane
@@ -167,50 +167,32 @@ __device__ __forceinline__ bool radix_advance(RadixState& st, const uint32_t* se
 // NT threads (gt = thread index in the group; warp 0 of the group scans).
 // Precondition: n > k, group synchronised, mm = {min, max} of the keys.
 // Returns T such that exactly k keys are >= T.
-template <int NT, int BAR>
+template <int NT>
 __device__ uint64_t group_select(const uint64_t* cand, uint32_t n, uint32_t k, const unsigned long long* mm,
-                                 uint32_t* hist, uint32_t* sel, int gt) {
+                                 uint32_t* hist, uint32_t* sel, int gt, uint32_t bar) {
   RadixState st = radix_start(mm[0], mm[1], k);
 #pragma unroll 1
   while (true) {
     for (int i = gt; i < 256; i += NT) hist[i] = 0u;
-    group_sync<NT, BAR>();
+    group_sync<NT>(bar);
     radix_hist<NT>(cand, n, st, hist, gt);
-    group_sync<NT, BAR>();
+    group_sync<NT>(bar);
     if (gt < 32) find_digit_warp(hist, st.krem, sel);
-    group_sync<NT, BAR>();
+    group_sync<NT>(bar);
     if (radix_advance(st, sel)) break;
   }
   return st.prefix;
 }
 
-// Cheap safe cut for a filling buffer: one 8-bit window just below the keys'
-// common prefix; keeps every key whose digit is >= the digit holding the
-// k-th largest key. At least k keys survive (so no key of the final top k is
-// dropped); *kept returns how many. Precondition as for group_select.
-template <int NT, int BAR>
-__device__ uint64_t group_cut(const uint64_t* cand, uint32_t n, uint32_t k, const unsigned long long* mm,
-                              uint32_t* hist, uint32_t* sel, int gt, uint32_t* kept) {
-  RadixState st = radix_start(mm[0], mm[1], k);
-  for (int i = gt; i < 256; i += NT) hist[i] = 0u;
-  group_sync<NT, BAR>();
-  radix_hist<NT>(cand, n, st, hist, gt);
-  group_sync<NT, BAR>();
-  if (gt < 32) find_digit_warp(hist, st.krem, sel);
-  group_sync<NT, BAR>();
-  *kept = sel[1] + sel[2];
-  const int width = window_width(st.top);
-  return st.prefix | (static_cast<uint64_t>(sel[0]) << (64 - st.top - width));
-}
-
 // Exclusive offset of this warp's count among the NT/32 warps of a group,
 // and the group total. wsum: NT/32 words; one group barrier inside, and the
 // caller must pass another barrier before wsum is written again.
-template <int NT, int BAR>
-__device__ __forceinline__ uint32_t group_warp_offset(uint32_t wcount, uint32_t* wsum, uint32_t* total, int gt) {
+template <int NT>
+__device__ __forceinline__ uint32_t group_warp_offset(uint32_t wcount, uint32_t* wsum, uint32_t* total, int gt,
+                                                      uint32_t bar) {
   const int gw = gt >> 5;
   if ((gt & 31) == 0) wsum[gw] = wcount;
-  group_sync<NT, BAR>();
+  group_sync<NT>(bar);
   uint32_t base = 0, tot = 0;
 #pragma unroll
   for (int k = 0; k < NT / 32; ++k) {
@@ -226,8 +208,9 @@ __device__ __forceinline__ uint32_t group_warp_offset(uint32_t wcount, uint32_t*
 // ends holding the number kept. MAXPER >= ceil(n / NT). The keys are held in
 // registers, so the packing is in place; output slots come from per-warp
 // ballot counts and one offset scan (no returning atomics in the loop).
-template <int NT, int BAR, int MAXPER>
-__device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* counter, uint32_t* wsum, int gt) {
+template <int NT, int MAXPER>
+__device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* counter, uint32_t* wsum, int gt,
+                              uint32_t bar) {
   const int lane = threadIdx.x & 31;
   uint64_t v[MAXPER];
   uint32_t m[MAXPER];
@@ -244,14 +227,53 @@ __device__ void group_compact(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* 
     cnt += static_cast<uint32_t>(__popc(m[j]));
   }
   uint32_t total = 0;
-  uint32_t base = group_warp_offset<NT, BAR>(cnt, wsum, &total, gt);  // every load is done past this barrier
+  uint32_t base = group_warp_offset<NT>(cnt, wsum, &total, gt, bar);  // every load is done past this barrier
 #pragma unroll
   for (int j = 0; j < MAXPER; ++j) {
     if ((m[j] >> lane) & 1u) cand[base + __popc(m[j] & lanemask_lt())] = v[j];
     base += static_cast<uint32_t>(__popc(m[j]));
   }
   if (gt == 0) *counter = total;
-  group_sync<NT, BAR>();
+  group_sync<NT>(bar);
+}
+
+// The same in chunks of NT * PER keys, for buffers longer than the registers
+// can hold at once: a key only moves to a lower index, and a chunk is loaded
+// into registers before any of its keys is written, so packing in place
+// chunk by chunk is safe.
+template <int NT, int PER>
+__device__ void group_compact_chunked(uint64_t* cand, uint32_t n, uint64_t T, uint32_t* counter, uint32_t* wsum,
+                                      int gt, uint32_t bar) {
+  const int lane = threadIdx.x & 31;
+  uint32_t base_all = 0;
+#pragma unroll 1
+  for (uint32_t c0 = 0; c0 < n; c0 += NT * PER) {
+    uint64_t v[PER];
+    uint32_t m[PER];
+    uint32_t cnt = 0;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const uint32_t i = c0 + gt + j * NT;
+      v[j] = (i < n) ? cand[i] : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const uint32_t i = c0 + gt + j * NT;
+      m[j] = __ballot_sync(0xFFFFFFFFu, (i < n) && (v[j] >= T));
+      cnt += static_cast<uint32_t>(__popc(m[j]));
+    }
+    uint32_t total = 0;
+    uint32_t base = base_all + group_warp_offset<NT>(cnt, wsum, &total, gt, bar);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      if ((m[j] >> lane) & 1u) cand[base + __popc(m[j] & lanemask_lt())] = v[j];
+      base += static_cast<uint32_t>(__popc(m[j]));
+    }
+    base_all += total;
+    group_sync<NT>(bar);  // wsum is rewritten by the next chunk
+  }
+  if (gt == 0) *counter = base_all;
+  group_sync<NT>(bar);
 }
 
 // Survivor count (keys >= T) of src[lo, hi), by one warp over consecutive
@@ -315,8 +337,8 @@ __device__ __forceinline__ uint32_t half16(const uint32_t* a, uint32_t d) {
 // fetches what is written for the key (issued for all of a thread's keys
 // before any store), emit.store(rank, value) writes it, emit.pad(i) fills
 // ranks n..2047 when n < 2048. tmp and tmpd hold 256 * KPT entries.
-// 256 threads (t = 0..255) synchronised by barrier BAR; kmin <= every key <=
-// kmax. Instead of a sorting network (which on 256 threads is bound by
+// 256 threads (t = 0..255, their index in the group; the group is
+// warp-aligned) synchronised by barrier `bar`; kmin <= every key <= kmax. Instead of a sorting network (which on 256 threads is bound by
 // shared-memory traffic or shuffle latency at tens of thousands of cycles for
 // 2048 64-bit keys), keys are counted into 4096 buckets, scattered bucket by
 // bucket, and each key's rank is the number of keys in higher buckets plus
@@ -332,10 +354,10 @@ __device__ __forceinline__ uint32_t half16(const uint32_t* a, uint32_t d) {
 // When the score range is empty or not finite the 12 key bits below the
 // common prefix of kmin and kmax are used instead (equal scores then spread
 // by position).
-template <int BAR, int KPT, class Emit>
+template <int KPT, class Emit>
 __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n, uint64_t kmin, uint64_t kmax,
-                                                const RankScratch sc, Emit& emit) {
-  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+                                                const RankScratch sc, Emit& emit, int t, uint32_t bar) {
+  const int lane = t & 31, w = t >> 5;
   {  // clear cnt and fill (2048 words each) with 16-byte stores
     uint4* c4 = reinterpret_cast<uint4*>(sc.cnt);
     uint4* f4 = reinterpret_cast<uint4*>(sc.fill);
@@ -371,11 +393,11 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
     k[j] = i < n ? keys[i] : 0ull;
     d[j] = bucket(k[j]);
   }
-  group_sync<256, BAR>();
+  group_sync<256>(bar);
 #pragma unroll
   for (int j = 0; j < KPT; ++j)
     if (t + 256 * j < n) atomicAdd(&sc.cnt[d[j] >> 1], 1u << ((d[j] & 1u) * 16u));
-  group_sync<256, BAR>();
+  group_sync<256>(bar);
   // Exclusive scan in descending bucket order; thread t owns words
   // 2047-8t down to 2040-8t, i.e. buckets 4095-16t down to 4080-16t (in a
   // word the odd bucket, high half, comes first).
@@ -393,7 +415,7 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
       if (lane >= off) incl += v;
     }
     if (lane == 31) sc.wsum[w] = incl;
-    group_sync<256, BAR>();
+    group_sync<256>(bar);
     uint32_t base = incl - tot;
     for (int q = 0; q < w; ++q) base += sc.wsum[q];
 #pragma unroll
@@ -404,7 +426,7 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
       base = lo + (c[j] & 0xFFFFu);
     }
   }
-  group_sync<256, BAR>();
+  group_sync<256>(bar);
   {  // scatter: all slot atomics first, then the stores that need them
     uint32_t slot[KPT];
 #pragma unroll
@@ -421,7 +443,7 @@ __device__ __forceinline__ void block_rank_emit(const uint64_t* keys, uint32_t n
         sc.tmpd[slot[j]] = static_cast<uint16_t>(d[j]);
       }
   }
-  group_sync<256, BAR>();
+  group_sync<256>(bar);
   // In-bucket ranks. First pass: the first four keys of every bucket, as
   // straight-line code over all of a thread's keys (their load chains
   // overlap); second pass: the rest of the rare buckets holding more.

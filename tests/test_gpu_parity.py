@@ -181,21 +181,26 @@ def test_partial_merge_equals_direct(pkg):
     assert np.array_equal(merged.cpu().numpy(), direct)
 
 
-def test_merge_out_of_range_position_is_missing(pkg):
+@pytest.mark.parametrize("nparts", [1, 2])
+def test_merge_out_of_range_position_is_missing(pkg, nparts):
     """A candidate position past the row's block-table span is treated as
-    missing by the merge (no read past the row) and flagged."""
+    missing by the merge (no read past the row) and flagged. The lists stay
+    best-first: the corrupted entry is row 0's last (worst) candidate; with
+    two parts the second list is empty (all missing)."""
     w = workloads().custom([3000, 5000], seed=14)
     d = w.to("cuda")
     direct = run(pkg, w)
-    cs, cp = pkg.indexer_partial(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, 0, 1 << 30)
-    cp[0, 0] = w.max_pages * 64 + 5  # the best candidate of row 0 now points past its pages
+    cs = torch.full((nparts, 2, 2048), float("-inf"), dtype=torch.float32, device="cuda")
+    cp = torch.full((nparts, 2, 2048), -1, dtype=torch.int32, device="cuda")
+    pkg.indexer_partial(d.q, d.k_cache, d.weights, d.seq_lens, d.block_table, 0, 1 << 30, cs[0], cp[0])
+    cp[0, 0, 2047] = w.max_pages * 64 + 5  # row 0's worst candidate now points past its pages
     pkg.device_status(0, clear=True)
-    merged = pkg.indexer_merge(cs.unsqueeze(0), cp.unsqueeze(0), d.seq_lens, d.block_table)
+    merged = pkg.indexer_merge(cs, cp, d.seq_lens, d.block_table)
     torch.cuda.synchronize()
     assert pkg.device_status(0) & pkg.DSA_STATUS_BAD_PAGE
     m = merged.cpu().numpy()
     assert np.array_equal(m[1], direct[1])
-    assert np.array_equal(m[0, :-1], direct[0, 1:]) and m[0, -1] == -1
+    assert np.array_equal(m[0, :-1], direct[0, :-1]) and m[0, -1] == -1
 
 
 def test_partial_unaligned_ranges(pkg):
