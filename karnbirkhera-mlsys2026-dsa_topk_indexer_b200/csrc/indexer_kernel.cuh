@@ -157,24 +157,14 @@ __device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, i
 
 __device__ unsigned int g_dsa_status;
 
-// d0 += a0 * b0 and d1 += a1 * b1 in one packed fp32x2 FMA.
-__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rb, {%4, %5};\n\t"
-      "mov.b64 rc, {%0, %1};\n\t"
-      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rc;\n\t}"
-      : "+f"(d0), "+f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-// acc[h] for 32 heads [h0, h0+32): s[] += w_h * relu(sgn * acc_h), eight
-// independent accumulators. The per-key scale is applied by the caller once
-// to the sum: relu(scale * x) = |scale| * relu(sign(scale) * x).
+// acc[h] for 32 heads [h0, h0+32): s[] += w_h * relu(sgn * acc_h) with
+// packed fp32x2 FMAs into four independent accumulator pairs. The per-key
+// scale is applied by the caller once to the sum: relu(scale * x) =
+// |scale| * relu(sign(scale) * x). relu is fmaxf(x, 0) (NaN -> 0), as in the
+// reference epilogue (solution/cuda/kernel.cu:423-430).
 template <bool kNeg>
 __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], const float* s_w, int h0,
-                                                 float (&s)[8]) {
+                                                 float2 (&s)[4]) {
   const float4* w4 = reinterpret_cast<const float4*>(s_w + h0);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -185,10 +175,30 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
       const float v = __uint_as_float(acc[4 * j + e]);
       r[e] = fmaxf(kNeg ? -v : v, 0.f);
     }
-    const int a = (j & 1) * 4;
-    ffma2(s[a + 0], s[a + 1], w.x, w.y, r[0], r[1]);
-    ffma2(s[a + 2], s[a + 3], w.z, w.w, r[2], r[3]);
+    const int a = (j & 1) * 2;
+    s[a] = __ffma2_rn(make_float2(w.x, w.y), make_float2(r[0], r[1]), s[a]);
+    s[a + 1] = __ffma2_rn(make_float2(w.z, w.w), make_float2(r[2], r[3]), s[a + 1]);
   }
+}
+
+// Score of this thread's key from its 64 TMEM accumulator columns at `ta`
+// (one query's heads): sum_h w_h * relu(scale * acc_h). The summation order
+// is fixed (four packed accumulator pairs, then a pairwise tree), so every
+// kernel that calls this produces bit-identical scores.
+__device__ __forceinline__ float key_score(uint32_t ta, const float* s_w, float scale) {
+  uint32_t a[32];
+  float2 s[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  ptx::tmem_ld_32x32b_x32_sync(ta, a);
+  if (scale >= 0.f)
+    head_reduce_half<false>(a, s_w, 0, s);
+  else
+    head_reduce_half<true>(a, s_w, 0, s);
+  ptx::tmem_ld_32x32b_x32_sync(ta + 32u, a);
+  if (scale >= 0.f)
+    head_reduce_half<false>(a, s_w, 32, s);
+  else
+    head_reduce_half<true>(a, s_w, 32, s);
+  return (((s[0].x + s[0].y) + (s[1].x + s[1].y)) + ((s[2].x + s[2].y) + (s[3].x + s[3].y))) * fabsf(scale);
 }
 
 // Cluster-wide exact selection of the best 2048 of all candidates held by the
@@ -602,26 +612,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!aborted) {
           __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
           ptx::tc_fence_after();
-          float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          {
-            uint32_t acc[32];
-            const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(buf * kHeads);
-            ptx::tmem_ld_32x32b_x32_sync(ta, acc);
-            if (scale >= 0.f)
-              head_reduce_half<false>(acc, s_w, 0, sums);
-            else
-              head_reduce_half<true>(acc, s_w, 0, sums);
-            ptx::tmem_ld_32x32b_x32_sync(ta + 32u, acc);
-            if (scale >= 0.f)
-              head_reduce_half<false>(acc, s_w, 32, sums);
-            else
-              head_reduce_half<true>(acc, s_w, 32, sums);
-          }
+          score = key_score(tmem + t_lane + static_cast<uint32_t>(buf * kHeads), s_w, scale);
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
-          score = (((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]))) *
-                  fabsf(scale);
         }
       }
       const int64_t pos = static_cast<int64_t>(pg_first + 2 * i) * kPage + row;

@@ -7,14 +7,21 @@
 //   warp 0      TMA producer: the four query boxes once, then per tile two
 //               8 KB page boxes and two 256 B scale rows into a 4-stage ring;
 //   warp 1      TMEM owner and MMA issuer: D[128 keys x 256] (fp32 in TMEM,
-//               2 buffers) = K_tile[128 x 128 e4m3] . Q[256 x 128 e4m3]^T as
-//               four tcgen05.mma kind::f8f6f4 (K = 32 each);
-//   warps 2..17 four epilogue groups of four warps, group j = query row j:
-//               thread = TMEM lane = key; tcgen05.ld of its 64 head columns
-//               of query j, relu / head weight / scale in registers, then the
-//               row's own threshold filter and candidate buffer (cut to the
-//               best 2048 when nearly full), synchronised per group only.
-// After the stream two 256-thread pairs of groups take two rows each: exact
+//               one buffer per tile parity) = K_tile[128 x 128 e4m3] .
+//               Q[256 x 128 e4m3]^T as four tcgen05.mma kind::f8f6f4 (K = 32);
+//   warps 2..17 sixteen epilogue warps: warp (parity, pair, quarter) takes the
+//               tiles of one parity, the two rows of one pair, and the 32 keys
+//               of one TMEM lane quarter (thread = key). Per tile it waits,
+//               reads the key scales and releases the stage once, then scores
+//               both rows from their 64 head columns (relu / head weight /
+//               scale in registers) and appends the keys above each row's
+//               threshold to that row's candidate buffer, cut to the best
+//               2048 when nearly full. The eight warps of a pair (both
+//               parities) meet only at those checks.
+// Scoring two rows per warp shares every per-tile wait, stage release and
+// TMEM hand-off between them; the math itself (64 max + 32 packed FMA per key
+// and row) is what bounds the kernel.
+// After the stream each pair's 256 threads take its two rows in turn: exact
 // radix select down to 2048 when more remain, then the bucket ordering and
 // the translation to physical slots (the same primitives as the per-row
 // kernel). Scores never go to HBM.
@@ -37,7 +44,7 @@ namespace dsa {
 
 constexpr int kPQ = kGroupRows;                    // query rows per CTA (4)
 constexpr int kPStages = 4;                        // K ring stages
-constexpr int kPWarps = 2 + 4 * kPQ;               // producer, MMA, 4 epilogue warps per row
+constexpr int kPWarps = 2 + 16;                    // producer, MMA, 16 epilogue warps
 constexpr int kPThreads = 32 * kPWarps;            // 576
 constexpr int kPCap = 3584;                        // candidate keys per row
 constexpr int kPBufCols = kPQ * kHeads;            // TMEM columns of one tile (N = 256)
@@ -74,15 +81,18 @@ enum PRowWord : int {
 // Shared misc words (uint32 at kPOffMisc + 128 * kPQ).
 enum PSharedWord : int { kPTmem = 0, kPAbort = 1, kPBad = 2 };
 
-// Named barriers: 1..4 the row groups (128 threads), 5..6 the tail pairs (256).
-constexpr int kPBarRow0 = 1;
-constexpr int kPBarPair0 = 5;
+// Named barriers 1..2: the 256 epilogue threads of row pair 0 / 1 (both
+// tile parities), at the buffer checks and in the tail.
+constexpr int kPBarPair0 = 1;
+static_assert(kPQ == 4, "two row pairs of two rows");
 
 struct PrefillParams {
   const int32_t* group_order;  // [ceil(B/4)] group served by CTA c (longest first), or null
   int32_t* handled;            // [B] out: 1 = row served here, 0 = left to the per-row kernel
 };
 
+// 18 warps: five of them share one SM sub-partition's 16384 registers, so
+// 96 registers per thread is the ceiling.
 template <int kMode>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
@@ -131,14 +141,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   // ---- do the rows share their pages? ----
   {
+    int npg[kPQ];  // pages whose entries must match: the row's visible pages
+    int npg_max = 0;
+#pragma unroll
+    for (int j = 0; j < kPQ; ++j) {
+      npg[j] = j == ref ? 0 : static_cast<int>((row_hi(j) + kPage - 1) / kPage);
+      npg_max = npg[j] > npg_max ? npg[j] : npg_max;
+    }
     bool bad = false;
-#pragma unroll 1
-    for (int j = 0; j < nq; ++j) {
-      if (j == ref) continue;
-      const int32_t* bt_j = p.block_table + static_cast<int64_t>(r0 + j) * p.max_pages;
-      const int npg = static_cast<int>((row_hi(j) + kPage - 1) / kPage);  // the row's visible pages
-      for (int pg = page_lo + static_cast<int>(threadIdx.x); pg < npg; pg += kPThreads)
-        bad |= bt_j[pg] != bt_ref[pg];
+    for (int pg = page_lo + static_cast<int>(threadIdx.x); pg < npg_max; pg += kPThreads) {
+      const int32_t r = bt_ref[pg];
+#pragma unroll
+      for (int j = 0; j < kPQ; ++j)
+        if (pg < npg[j]) bad |= p.block_table[static_cast<int64_t>(r0 + j) * p.max_pages + pg] != r;
     }
     if (__syncthreads_or(bad ? 1 : 0)) {
       if (threadIdx.x < static_cast<unsigned>(nq)) pp.handled[r0 + threadIdx.x] = 0;
@@ -159,11 +174,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, 1 + 4 * kPQ);  // MMA commit + every epilogue warp
+      ptx::mbar_init(bar_empty + 8 * s, 1 + 8);  // MMA commit + the 8 warps of the tile's parity
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(bar_tfull + 8 * i, 1);
-      ptx::mbar_init(bar_tempty + 8 * i, 4 * kPQ);
+      ptx::mbar_init(bar_tempty + 8 * i, 8);
     }
     ptx::mbar_init(bar_q, 1);
     ptx::fence_mbar_init();
@@ -282,48 +297,84 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mma_issued = i + 1;
     }
   } else {
-    // ===================== epilogue: group j = query row j =====================
-    const int j = (warp - 2) >> 2;
-    const int q4 = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q4 * 32 + lane;
-    const int gt = threadIdx.x - 64 - 128 * j;  // 0..127 within the group
-    const uint32_t bar_row = kPBarRow0 + j;
+    // ===================== epilogue =====================
+    const int ew = warp - 2;
+    const int par = ew >> 3;                    // tiles of this parity
+    const int qp = (ew >> 2) & 1;               // rows 2*qp and 2*qp + 1
+    const int q4 = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = q4 * 32 + lane;             // key of the tile
+    const int gt = ((ew & 3) + 4 * par) * 32 + lane;  // 0..255 within the pair's eight warps
+    const uint32_t bar_qp = kPBarPair0 + qp;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
-    const float* s_w = reinterpret_cast<const float*>(smem + kPOffW) + j * kHeads;
-    uint64_t* cand = reinterpret_cast<uint64_t*>(smem + kPOffCand) + j * kPCap;
-    uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kPOffHist) + j * 256;
-    uint32_t* rmisc = reinterpret_cast<uint32_t*>(smem + kPOffMisc + 128 * j);
-    volatile uint32_t* rmisc_v = rmisc;
-    unsigned long long* mm = reinterpret_cast<unsigned long long*>(rmisc + kPMM);
-    const int64_t key_hi = row_hi(j);
-    uint64_t thr = 0;  // keys below thr can no longer reach the row's top 2048
+    const int jA = 2 * qp, jB = 2 * qp + 1;
+    const float* w_A = reinterpret_cast<const float*>(smem + kPOffW) + jA * kHeads;
+    const float* w_B = w_A + kHeads;
+    uint64_t* cand_A = reinterpret_cast<uint64_t*>(smem + kPOffCand) + jA * kPCap;
+    uint64_t* cand_B = cand_A + kPCap;
+    uint32_t* misc_A = reinterpret_cast<uint32_t*>(smem + kPOffMisc + 128 * jA);
+    uint32_t* misc_B = misc_A + 32;
+    // Key positions fit in 32 bits: max_pages * 64 <= INT32_MAX (host check).
+    const uint32_t hi_A = static_cast<uint32_t>(row_hi(jA)), hi_B = static_cast<uint32_t>(row_hi(jB));
+    const uint32_t lo32 = static_cast<uint32_t>(lo);
+    const int n_pairs_full = n_tiles >> 1;
+    uint64_t thr_A = 0, thr_B = 0;  // keys below thr can no longer reach the row's top 2048
+    uint32_t nb_A = 0, nb_B = 0;    // candidates counted at the last check
+    uint32_t slot = 0;              // rotating append counter of the current interval (both rows)
     int since = 0;
-    int check_every = kPCap / kTileKeys;
-    // Same append protocol as the per-row kernel: keys of the current check
-    // interval take slots n_base + (rotating counter `slot`), each warp
-    // storing a tile's keys one tile late once its slot atomic has returned.
-    uint32_t n_base = 0, slot = 0, pm = 0, pbase = 0;
-    int pleader = 0;
-    bool pkeep = false;
-    uint64_t pkey = 0;
-    auto flush = [&]() {
-      if (pm) {
-        const uint32_t pbv = __shfl_sync(0xFFFFFFFFu, pbase, pleader);
-        if (pkeep) cand[n_base + pbv + __popc(pm & lanemask_lt())] = pkey;
+    int check_every = kPCap / (2 * kTileKeys);  // tile pairs between checks
+    // Same append protocol as the per-row kernel, per row: keys of the
+    // current interval take slots nb + (rotating counter `slot`), each warp
+    // storing a tile's keys one tile later, once its slot atomic has returned.
+    struct Pending {
+      uint32_t m = 0, base = 0;
+      int leader = 0;
+      bool keep = false;
+      uint64_t key = 0;
+    };
+    Pending pa, pb;
+    auto flush = [&](Pending& q, uint64_t* cand, uint32_t nb) {
+      if (q.m) {
+        const uint32_t b0 = __shfl_sync(0xFFFFFFFFu, q.base, q.leader);
+        if (q.keep) cand[nb + b0 + __popc(q.m & lanemask_lt())] = q.key;
       }
-      pm = 0u;
+      q.m = 0u;
+    };
+    auto append = [&](Pending& q, uint32_t* misc, uint64_t key, bool keep) {
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
+      q.m = m;
+      q.keep = keep;
+      q.key = key;
+      if (m) {
+        q.leader = __ffs(m) - 1;
+        q.base = 0u;
+        if (lane == q.leader) q.base = atomicAdd(misc + kPRot + slot, static_cast<uint32_t>(__popc(m)));
+      }
+    };
+    // Cut of one row's buffer to exactly its best 2048 (all 256 threads).
+    auto cut = [&](uint64_t* cand, uint32_t* misc, uint32_t n, int j) -> uint64_t {
+      unsigned long long* mm = reinterpret_cast<unsigned long long*>(misc + kPMM);
+      if (gt == 0) {
+        mm[0] = ~0ull;
+        mm[1] = 0ull;
+      }
+      ptx::named_bar(bar_qp, 256);
+      group_minmax<256>(cand, n, mm, gt, bar_qp);
+      uint32_t* hist = reinterpret_cast<uint32_t*>(smem + kPOffHist) + j * 256;
+      const uint64_t T = group_select<256>(cand, n, kTopK, mm, hist, misc + kPSel, gt, bar_qp);
+      group_compact_chunked<256, 8>(cand, n, T, misc + kPCount, misc + kPWsum, gt, bar_qp);
+      return T;
     };
     // A warp whose wait gave up (`aborted`, warp-uniform) stops touching the
     // pipeline but keeps walking the same tile schedule with no keys, so it
-    // still meets its group at every check barrier.
+    // still meets its pair at every check barrier.
 #pragma unroll 1
-    for (int i = 0; i < n_tiles; ++i) {
+    for (int i = par; i < n_tiles; i += 2) {
       const int s = i % kPStages;
       const uint32_t ph = static_cast<uint32_t>(i / kPStages) & 1u;
-      const int buf = i & 1;
-      const int64_t tile_key0 = static_cast<int64_t>(page_lo + 2 * i) * kPage;
-      const bool live = tile_key0 < key_hi && tile_key0 + kTileKeys > lo;  // tile holds keys of this row
-      float score = 0.f;
+      const uint32_t tile_key0 = static_cast<uint32_t>(page_lo + 2 * i) * kPage;
+      const bool live_A = tile_key0 < hi_A && tile_key0 + kTileKeys > lo32;  // the tile holds keys of row A
+      const bool live_B = tile_key0 < hi_B && tile_key0 + kTileKeys > lo32;
+      float sc_A = 0.f, sc_B = 0.f;
       if (!aborted) {
         const bool ok =
             ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
@@ -337,81 +388,69 @@ __global__ void __launch_bounds__(kPThreads, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
         const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
-        const bool ok =
-            ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
+        const bool ok = ptx::mbar_wait(bar_tfull + 8 * par, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
+                                       p.wait_ns);
         if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
         if (!aborted) {
           __syncwarp();
           ptx::tc_fence_after();
-          if (live) {
-            float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            uint32_t acc[32];
-            const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(buf * kPBufCols + j * kHeads);
-            ptx::tmem_ld_32x32b_x32_sync(ta, acc);
-            if (scale >= 0.f)
-              head_reduce_half<false>(acc, s_w, 0, sums);
-            else
-              head_reduce_half<true>(acc, s_w, 0, sums);
-            ptx::tmem_ld_32x32b_x32_sync(ta + 32u, acc);
-            if (scale >= 0.f)
-              head_reduce_half<false>(acc, s_w, 32, sums);
-            else
-              head_reduce_half<true>(acc, s_w, 32, sums);
-            score = (((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]))) *
-                    fabsf(scale);
-          }
+          const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(par * kPBufCols);
+          if (live_A) sc_A = key_score(ta + static_cast<uint32_t>(jA * kHeads), w_A, scale);
+          if (live_B) sc_B = key_score(ta + static_cast<uint32_t>(jB * kHeads), w_B, scale);
           ptx::tc_fence_before();
           __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * buf);
+          if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * par);
         }
       }
-      const int64_t pos = tile_key0 + row;
-      const bool valid = !aborted && pos >= lo && pos < key_hi;
-      const uint64_t key = pack_key(score, static_cast<uint32_t>(pos));
-      const bool keep = valid && key >= thr;
-      flush();
-      const uint32_t m = __ballot_sync(0xFFFFFFFFu, keep);
-      pm = m;
-      pkeep = keep;
-      pkey = key;
-      if (m) {
-        pleader = __ffs(m) - 1;
-        pbase = 0u;
-        if (lane == pleader) pbase = atomicAdd(rmisc + kPRot + slot, static_cast<uint32_t>(__popc(m)));
-      }
-      // Every check_every tiles the row's buffer may be nearly full: the
-      // group meets, reads the interval's count, moves to the next counter
-      // and clears the one used two intervals ago; when fewer than two tiles
-      // of room are left it cuts the buffer to exactly the best 2048. The
-      // schedule depends only on tile counts, so the group's four warps take
-      // the same barriers.
-      if (++since == check_every && i + 1 < n_tiles) {
+      const uint32_t pos = tile_key0 + static_cast<uint32_t>(row);
+      const bool in_range = !aborted && pos >= lo32;
+      const uint64_t key_A = pack_key(sc_A, pos);
+      const uint64_t key_B = pack_key(sc_B, pos);
+      flush(pa, cand_A, nb_A);
+      append(pa, misc_A, key_A, in_range && pos < hi_A && key_A >= thr_A);
+      flush(pb, cand_B, nb_B);
+      append(pb, misc_B, key_B, in_range && pos < hi_B && key_B >= thr_B);
+      // Every check_every tile pairs the buffers may be nearly full: the
+      // pair's eight warps meet, read each row's interval count, move to the
+      // next counter and clear the one used two intervals ago; a row with
+      // fewer than two tile pairs of room left is cut to exactly its best
+      // 2048. The schedule depends only on tile counts, so both parities take
+      // the same checks.
+      if (++since == check_every) {
         since = 0;
-        flush();
-        ptx::named_bar(bar_row, 128);
-        const uint32_t n = n_base + rmisc_v[kPRot + slot];
-        if (gt == 0) rmisc[kPRot + (slot + 2u) % 3u] = 0u;
-        n_base = n;
-        slot = (slot + 1u) % 3u;
-        if (n > static_cast<uint32_t>(kPCap - 2 * kTileKeys)) {
+        if ((i >> 1) < n_pairs_full) {
+          flush(pa, cand_A, nb_A);
+          flush(pb, cand_B, nb_B);
+          ptx::named_bar(bar_qp, 256);
+          const uint32_t n_A = nb_A + reinterpret_cast<volatile uint32_t*>(misc_A)[kPRot + slot];
+          const uint32_t n_B = nb_B + reinterpret_cast<volatile uint32_t*>(misc_B)[kPRot + slot];
           if (gt == 0) {
-            mm[0] = ~0ull;
-            mm[1] = 0ull;
+            misc_A[kPRot + (slot + 2u) % 3u] = 0u;
+            misc_B[kPRot + (slot + 2u) % 3u] = 0u;
           }
-          ptx::named_bar(bar_row, 128);
-          group_minmax<128>(cand, n, mm, gt, bar_row);
-          const uint64_t T = group_select<128>(cand, n, kTopK, mm, hist, rmisc + kPSel, gt, bar_row);
-          group_compact_chunked<128, 8>(cand, n, T, rmisc + kPCount, rmisc + kPWsum, gt, bar_row);
-          thr = T;
-          n_base = rmisc_v[kPCount];
+          nb_A = n_A;
+          nb_B = n_B;
+          slot = (slot + 1u) % 3u;
+          if (n_A > static_cast<uint32_t>(kPCap - 4 * kTileKeys)) {
+            thr_A = cut(cand_A, misc_A, n_A, jA);
+            nb_A = reinterpret_cast<volatile uint32_t*>(misc_A)[kPCount];
+          }
+          if (n_B > static_cast<uint32_t>(kPCap - 4 * kTileKeys)) {
+            thr_B = cut(cand_B, misc_B, n_B, jB);
+            nb_B = reinterpret_cast<volatile uint32_t*>(misc_B)[kPCount];
+          }
+          const uint32_t room = kPCap - (nb_A > nb_B ? nb_A : nb_B);
+          check_every = static_cast<int>(room / (2 * kTileKeys));
         }
-        check_every = static_cast<int>((kPCap - n_base) / kTileKeys);
       }
     }
-    flush();
+    flush(pa, cand_A, nb_A);
+    flush(pb, cand_B, nb_B);
     if (gt == 0) {  // read after the barrier below
-      rmisc[kPFinal] = n_base;
-      rmisc[kPSel] = slot;  // the counter in use at the end (sel words are free now)
+      misc_A[kPFinal] = nb_A;
+      misc_A[kPSel] = slot;  // the counter in use at the end (sel words are free now)
+      misc_B[kPFinal] = nb_B;
+      misc_B[kPSel] = slot;
     }
   }
   // ---- end of the stream: drain, release TMEM ----
@@ -439,9 +478,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
   if (warp < 2) return;
 
-  // ---- tail: pair q2 (warps 2+8*q2 .. 9+8*q2) selects and orders rows 2*q2, 2*q2+1 ----
-  const int pair = (warp - 2) >> 3;
-  const int pt = threadIdx.x - 64 - 256 * pair;  // 0..255
+  // ---- tail: the eight warps of row pair `pair` select and order its two rows ----
+  const int pair = ((warp - 2) >> 2) & 1;
+  const int pt = ((((warp - 2) & 3) + 4 * ((warp - 2) >> 3)) * 32) + lane;  // 0..255 within the pair
   const uint32_t bar_pair = kPBarPair0 + pair;
   uint32_t* pmisc = reinterpret_cast<uint32_t*>(smem + kPOffMisc + 128 * (2 * pair));
   RankScratch sc;

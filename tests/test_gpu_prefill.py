@@ -18,6 +18,12 @@ from parity import check_all
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True)
+def _prefill_on(monkeypatch):
+    """The stage is opt-in (DSA_TOPK_PREFILL=1); these tests turn it on."""
+    monkeypatch.setenv("DSA_TOPK_PREFILL", "1")
+
+
 def _check(pkg, w, monkeypatch=None, prefill=True):
     if monkeypatch is not None and not prefill:
         monkeypatch.setenv("DSA_TOPK_PREFILL", "0")
