@@ -14,7 +14,9 @@ come from the PyTorch restatement (oracle/reference_torch.py).
 
 With --time it also times the reference kernel beside this library's on
 config 0 and config 3 (direct calls on the current stream, CUDA events,
-256 MB L2 flush before every call) and prints one JSON line per config.
+256 MB L2 flush before every call, about 1.5 s of calls per arm with the
+SM clocks and throttle reasons sampled meanwhile) and prints one JSON line
+per config. With --time-only it skips writing the fixtures.
 
 Run on a GPU machine:  python tests/golden/make_ref_golden.py [--time] [--out DIR]
 (--out writes the fixtures elsewhere, e.g. a folder the GPU machine returns.)
@@ -78,34 +80,54 @@ def make(ref, out_dir):
         print(path, os.path.getsize(path), "bytes", flush=True)
 
 
-def time_call(fn, flush, iters=20, warmup=3):
+def time_call(fn, flush, min_seconds=1.5, warmup=3):
+    """Median device time of fn() (CUDA events on the current stream, 256 MB
+    L2 flush before every call) over enough calls to run about min_seconds,
+    with the GPU's clocks sampled by nvidia-smi meanwhile (bench.py's
+    ClockSampler: reads only, changes no setting). Returns (ms, clocks)."""
+    from bench import ClockSampler  # repository root
     for _ in range(warmup):
         flush.zero_()
         fn()
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-    for a, b in ev:
+    a0, b0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(st)
+    for _ in range(5):
         flush.zero_()
-        a.record(st)
         fn()
-        b.record(st)
+    b0.record(st)
     torch.cuda.synchronize()
-    return sorted(a.elapsed_time(b) for a, b in ev)[iters // 2]
+    iters = max(20, int(min_seconds * 1e3 / max(a0.elapsed_time(b0) / 5, 1e-3)))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for a, b in ev:
+            flush.zero_()
+            a.record(st)
+            fn()
+            b.record(st)
+        torch.cuda.synchronize()
+    return sorted(a.elapsed_time(b) for a, b in ev)[iters // 2], dict(clk.summary(), calls=iters)
 
 
 def head_to_head(ref):
+    """Reference kernel vs this library on configs 0 and 3 (the configs the
+    reference's host code accepts), one JSON line per config with both arms'
+    clock records."""
     pkg = importlib.import_module("karnbirkhera-mlsys2026-dsa_topk_indexer_b200")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
     for idx in (0, 3):
         w = wl.config(idx, device="cuda")
         o_ref = torch.empty((w.batch, 2048), dtype=torch.int32, device="cuda")
         o_our = torch.empty_like(o_ref)
-        t_ref = time_call(lambda: ref.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, o_ref), flush)
-        t_our = time_call(lambda: pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table, o_our), flush)
+        t_ref, c_ref = time_call(lambda: ref.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table,
+                                                           o_ref), flush)
+        t_our, c_our = time_call(lambda: pkg.launch_topk_c(w.q, w.k_cache, w.weights, w.seq_lens, w.block_table,
+                                                           o_our), flush)
         same = float((o_ref == o_our).float().mean())
         print(json.dumps({"config": idx, "rows": w.batch, "reference_ms_median": t_ref, "ours_ms_median": t_our,
-                          "speedup": t_ref / t_our, "identical_slot_fraction": same}), flush=True)
+                          "speedup": t_ref / t_our, "identical_slot_fraction": same,
+                          "reference_clocks": c_ref, "ours_clocks": c_our}), flush=True)
         del w, o_ref, o_our
         torch.cuda.empty_cache()
 
@@ -114,6 +136,7 @@ if __name__ == "__main__":
     ref = build_ref.load_ref()
     out_dir = sys.argv[sys.argv.index("--out") + 1] if "--out" in sys.argv else HERE
     os.makedirs(out_dir, exist_ok=True)
-    make(ref, out_dir)
-    if "--time" in sys.argv:
+    if "--time-only" not in sys.argv:
+        make(ref, out_dir)
+    if "--time" in sys.argv or "--time-only" in sys.argv:
         head_to_head(ref)
