@@ -162,7 +162,14 @@ __device__ unsigned int g_dsa_status;
 // scale is applied by the caller once to the sum: relu(scale * x) =
 // |scale| * relu(sign(scale) * x). relu is fmaxf(x, 0) (NaN -> 0), as in the
 // reference epilogue (solution/cuda/kernel.cu:423-430).
-template <bool kNeg>
+//
+// kFast: the heads accumulated into s[1] and s[3] take x + |x| = 2 relu(x)
+// instead (an add on the FMA pipe rather than a max on the half-rate ALU
+// pipe); the caller halves those two accumulators, which gives exactly the
+// same value, because scaling by 2 and 1/2 is exact in fp32. Only a NaN
+// accumulator (possible only from NaN input bytes) behaves differently: it
+// turns the sum into NaN, and the caller then recomputes with kFast = false.
+template <bool kNeg, bool kFast>
 __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], const float* s_w, int h0,
                                                  float2 (&s)[4]) {
   const float4* w4 = reinterpret_cast<const float4*>(s_w + h0);
@@ -173,7 +180,8 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float v = __uint_as_float(acc[4 * j + e]);
-      r[e] = fmaxf(kNeg ? -v : v, 0.f);
+      const float x = kNeg ? -v : v;
+      r[e] = (kFast && e >= 2) ? x + fabsf(x) : fmaxf(x, 0.f);
     }
     const int a = (j & 1) * 2;
     s[a] = __ffma2_rn(make_float2(w.x, w.y), make_float2(r[0], r[1]), s[a]);
@@ -181,24 +189,34 @@ __device__ __forceinline__ void head_reduce_half(const uint32_t (&acc)[32], cons
   }
 }
 
-// Score of this thread's key from its 64 TMEM accumulator columns at `ta`
-// (one query's heads): sum_h w_h * relu(scale * acc_h). The summation order
-// is fixed (four packed accumulator pairs, then a pairwise tree), so every
-// kernel that calls this produces bit-identical scores.
-__device__ __forceinline__ float key_score(uint32_t ta, const float* s_w, float scale) {
+template <bool kFast>
+__device__ __forceinline__ float key_score_pass(uint32_t ta, const float* s_w, float scale) {
   uint32_t a[32];
   float2 s[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   ptx::tmem_ld_32x32b_x32_sync(ta, a);
   if (scale >= 0.f)
-    head_reduce_half<false>(a, s_w, 0, s);
+    head_reduce_half<false, kFast>(a, s_w, 0, s);
   else
-    head_reduce_half<true>(a, s_w, 0, s);
+    head_reduce_half<true, kFast>(a, s_w, 0, s);
   ptx::tmem_ld_32x32b_x32_sync(ta + 32u, a);
   if (scale >= 0.f)
-    head_reduce_half<false>(a, s_w, 32, s);
+    head_reduce_half<false, kFast>(a, s_w, 32, s);
   else
-    head_reduce_half<true>(a, s_w, 32, s);
-  return (((s[0].x + s[0].y) + (s[1].x + s[1].y)) + ((s[2].x + s[2].y) + (s[3].x + s[3].y))) * fabsf(scale);
+    head_reduce_half<true, kFast>(a, s_w, 32, s);
+  const float h = kFast ? 0.5f : 1.f;
+  return (((s[0].x + s[0].y) + h * (s[1].x + s[1].y)) + ((s[2].x + s[2].y) + h * (s[3].x + s[3].y))) *
+         fabsf(scale);
+}
+
+// Score of this thread's key from its 64 TMEM accumulator columns at `ta`
+// (one query's heads): sum_h w_h * relu(scale * acc_h). The summation order
+// is fixed (four packed accumulator pairs, then a pairwise tree), so every
+// kernel that calls this produces bit-identical scores. Called by the whole
+// warp (tcgen05.ld is warp-collective).
+__device__ __forceinline__ float key_score(uint32_t ta, const float* s_w, float scale) {
+  const float f = key_score_pass<true>(ta, s_w, scale);
+  if (__any_sync(0xFFFFFFFFu, f != f)) return key_score_pass<false>(ta, s_w, scale);  // NaN inputs: exact relu
+  return f;
 }
 
 // Cluster-wide exact selection of the best 2048 of all candidates held by the

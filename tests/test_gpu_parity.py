@@ -224,6 +224,18 @@ def test_deterministic_and_side_stream(pkg):
     assert np.array_equal(a, b)
 
 
+def test_nan_input_bytes_relu_to_zero(pkg):
+    """e4m3 NaN bytes (0x7F) in a key and in one query head: the affected
+    head products are NaN and relu maps them to 0, as the reference's
+    fmaxf(x, 0) epilogue does (the oracle: x > 0 ? x : 0)."""
+    w = workloads().custom([3000, 5000], seed=15)
+    page = int(w.block_table[0, 3])
+    w.k_cache[page, 10, 0, 5] = 0x7F           # one key of row 0
+    q8 = w.q.view(torch.uint8)
+    q8[1, 7, 3] = 0x7F                          # head 7 of row 1, every key
+    assert_parity(pkg, w)
+
+
 def test_bad_page_id_flags_status(pkg):
     """An out-of-range page id is zero-filled by the TMA bounds check and
     reported in the status word; the kernel does not fault."""
