@@ -178,9 +178,11 @@ int prepare_device(int* num_sms, int64_t* l2_bytes = nullptr) {
     if (prop.major != 10 || prop.minor != 0) return DSA_ERR_NO_DEVICE;
     d.num_sms = prop.multiProcessorCount;
     d.l2_bytes = prop.l2CacheSize;
-    const void* fns[3] = {reinterpret_cast<const void*>(&indexer_kernel<kModeTopK>),
+    const void* fns[5] = {reinterpret_cast<const void*>(&indexer_kernel<kModeTopK>),
                           reinterpret_cast<const void*>(&indexer_kernel<kModeScores>),
-                          reinterpret_cast<const void*>(&indexer_kernel<kModePartial>)};
+                          reinterpret_cast<const void*>(&indexer_kernel<kModePartial>),
+                          reinterpret_cast<const void*>(&indexer_kernel<kModeTopK, true>),
+                          reinterpret_cast<const void*>(&indexer_kernel<kModePartial, true>)};
     for (const void* f : fns) {
       if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess ||
           cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
@@ -372,6 +374,12 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   IndexerParams params = prm;
   int launches = 1;
   auto launch = [&](const IndexerParams& pp, int64_t rows, int g, cudaStream_t st) -> int {
+    // Two-class launches with in-kernel ranking use the instantiation that
+    // decides the split on the device.
+    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, IndexerParams) = indexer_kernel<kMode>;
+    if constexpr (kMode != kModeScores) {
+      if (pp.split_role >= 0) kern = indexer_kernel<kMode, true>;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(g * rows), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -384,7 +392,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, indexer_kernel<kMode>, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+    return cudaLaunchKernelEx(&cfg, kern, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
   };
 
   // Shared-sequence stage (DSA_TOPK_PREFILL=1): plan (row order + group
@@ -449,13 +457,32 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
         KernelTimer timer(stream);
         if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
-        IndexerParams lo = params;
-        if (order)
+        IndexerParams hi = params, lo = params;
+        int64_t hi_rows = R;
+        if (order) {
           lo.order = order + R;
-        else
+        } else if (kMode == kModeScores) {
           lo.order_base = static_cast<int32_t>(R);
-        if ((rc = launch(params, R, G, stream)) != DSA_OK) return rc;
+        } else {
+          // In-kernel ranking: the kernel itself decides, from the lengths,
+          // between this split and all rows at G in waves; the G launch then
+          // covers every rank and the other one may find nothing to do.
+          lo.order_base = static_cast<int32_t>(R);
+          hi.split_role = 0;
+          lo.split_role = 1;
+          for (IndexerParams* q : {&hi, &lo}) {
+            q->split_r = static_cast<int32_t>(R);
+            q->split_ghi = G;
+            q->split_glo = kGLow;
+            q->split_slots = 2 * num_sms;
+          }
+          hi_rows = prm.batch;
+        }
+        // The small-cluster launch goes first: when the split is taken its
+        // clusters get their slots before the G launch's surplus clusters
+        // (ranks >= R, which exit at once) are dispatched.
         if ((rc = launch(lo, prm.batch - R, kGLow, side)) != DSA_OK) return rc;
+        if ((rc = launch(hi, hi_rows, G, stream)) != DSA_OK) return rc;
         if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
         timer.stop();

@@ -124,17 +124,31 @@ struct IndexerParams {
   // [B] or null: rows whose entry is nonzero were served by the
   // shared-sequence kernel launched before this one and are skipped.
   const int32_t* handled = nullptr;
+  // Two-class launch with in-kernel ranking: role 0 is the launch at
+  // cluster size split_ghi over every rank, role 1 the launch at split_glo
+  // over ranks >= split_r. From the real lengths the kernel decides whether
+  // the split pays (split_beats_waves); if it does, role 0 serves ranks <
+  // split_r and role 1 the rest, else role 0 serves every rank (in waves,
+  // longest first) and role 1 exits. -1: no two-class launch.
+  int32_t split_role = -1;
+  int32_t split_r = 0, split_ghi = 0, split_glo = 0, split_slots = 0;
 };
 
 constexpr int kInKernelOrderMax = 256;  // rows ranked in-kernel at most
-static_assert(kCap * 8 >= kInKernelOrderMax * 4, "in-kernel row ranking scratch (candidate buffer)");
+static_assert(kCap * 8 >= kInKernelOrderMax * 8, "in-kernel row ranking scratch (candidate buffer)");
 
 // Longest-first rank -> row, computed by every CTA from the clamped lengths
 // (ties: smaller row first, as the plan kernel's counting sort would give
-// within a bucket). All kThreads threads; `scratch` holds batch ints.
-__device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, int32_t* scratch,
-                                           uint32_t* result) {
+// within a bucket). All kThreads threads; `scratch` holds 2 x batch ints.
+// kTwoClass: it also decides the two-class launch (*split = 1 if the split
+// pays, split_beats_waves).
+__device__ __forceinline__ bool split_beats_waves(const IndexerParams& p, const int32_t* sorted_tiles, int64_t total);
+
+template <bool kTwoClass>
+__device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, int32_t* scratch, uint32_t* result,
+                                           uint32_t* split) {
   const int64_t cap = static_cast<int64_t>(p.max_pages) * kPage;
+  int32_t* sorted_tiles = scratch + p.batch;
   for (int j = threadIdx.x; j < p.batch; j += kThreads) {
     int64_t l = p.seq_lens[j];
     l = l < 0 ? 0 : (l > cap ? cap : l);
@@ -150,9 +164,44 @@ __device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, i
       r += (lj > li || (lj == li && j < i)) ? 1 : 0;
     }
     if (r == target) *result = static_cast<uint32_t>(i);
+    if constexpr (kTwoClass) sorted_tiles[r] = li;
   }
   __syncthreads();
+  if constexpr (kTwoClass) {
+    if (threadIdx.x == 0) {
+      int64_t total = 0;
+      for (int j = 0; j < p.batch; ++j) total += scratch[j];
+      *split = split_beats_waves(p, sorted_tiles, total) ? 1u : 0u;
+    }
+    __syncthreads();
+  }
   return static_cast<int>(*result);
+}
+
+// Two-class launch or waves? Estimated makespans in tiles per CTA, from the
+// tile counts sorted longest first:
+//   split: one wave, max(t[0] / ghi, t[r] / glo) (the longest row of each class);
+//   waves: every row at ghi, longest first, slots / ghi clusters at a time:
+//          max(t[0] / ghi, (t[c-1] + t[c]) / ghi, total / slots) plus one more
+//          row tail (select and ordering, about kWaveTailTiles tiles of time).
+// Measured on B200: log-uniform 512..32k-key rows (64) run 45 us split vs
+// 51 us in waves; uniform 16k..131k-key rows (64) 0.20 ms split vs 0.16 ms
+// in waves.
+constexpr int64_t kWaveTailTiles = 25;
+
+__device__ __forceinline__ bool split_beats_waves(const IndexerParams& p, const int32_t* t, int64_t total) {
+  const int64_t ghi = p.split_ghi, glo = p.split_glo, slots = p.split_slots, B = p.batch, r = p.split_r;
+  auto ceil_div = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
+  const int64_t split = ceil_div(t[0], ghi) > ceil_div(t[r], glo) ? ceil_div(t[0], ghi) : ceil_div(t[r], glo);
+  const int64_t c = slots / ghi;
+  int64_t waves = ceil_div(t[0], ghi);
+  if (c >= 1 && c < B) {
+    const int64_t two = ceil_div(static_cast<int64_t>(t[c - 1]) + t[c], ghi);
+    waves = two > waves ? two : waves;
+  }
+  const int64_t fill = ceil_div(total, slots);
+  waves = (fill > waves ? fill : waves) + kWaveTailTiles;
+  return split < waves;
 }
 
 __device__ unsigned int g_dsa_status;
@@ -393,7 +442,10 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
   }
 }
 
-template <int kMode>
+// kTwoClass: one of the two launches of the two-class schedule with
+// in-kernel ranking (IndexerParams::split_role); a separate instantiation
+// so that the single-launch kernel carries none of it.
+template <int kMode, bool kTwoClass = false>
 __global__ void __launch_bounds__(kThreads, 2)
     indexer_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
                    const __grid_constant__ CUtensorMap tm_q, const IndexerParams p) {
@@ -421,10 +473,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t G = ptx::cluster_nctarank();
   const uint32_t rank = ptx::cluster_ctarank();
   const int b = p.order_base >= 0
-                    ? row_of_rank(p, p.order_base + static_cast<int>(blockIdx.x / G),
-                                  reinterpret_cast<int32_t*>(smem + kOffCand), misc_nv + kMiscSel)
+                    ? row_of_rank<kTwoClass>(p, p.order_base + static_cast<int>(blockIdx.x / G),
+                                             reinterpret_cast<int32_t*>(smem + kOffCand), misc_nv + kMiscSel,
+                                             misc_nv + kMiscSel + 1)
                     : (p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G));
   if (p.handled && p.handled[b]) return;  // uniform over the cluster, before any barrier or TMEM use
+  if constexpr (kTwoClass) {  // does this launch serve this rank? (uniform over the cluster)
+    const bool split = misc_nv[kMiscSel + 1] != 0u;
+    const int k = p.order_base + static_cast<int>(blockIdx.x / G);
+    if (p.split_role == 0 ? (split && k >= p.split_r) : !split) return;
+  }
 
   // ---- request geometry (identical in every thread) ----
   int64_t len = p.seq_lens[b];

@@ -275,6 +275,20 @@ def test_cluster_two_class_launch(pkg, split, monkeypatch):
     assert_parity(pkg, w)
 
 
+@pytest.mark.parametrize("kind", ["uniform", "loguniform"])
+def test_two_class_launch_decided_on_device(pkg, kind):
+    """64 rows, in-kernel ranking: the kernel decides between the two-class
+    split and all rows in waves from the lengths (uniform long rows take
+    waves, log-uniform ones the split); both must be parity-green."""
+    g = torch.Generator().manual_seed(81)
+    u = torch.rand(64, generator=g, dtype=torch.float64)
+    if kind == "uniform":
+        sl = (16384 + u * (131072 - 16384)).floor().to(torch.int32)
+    else:
+        sl = torch.exp(np.log(512) + u * (np.log(32768) - np.log(512))).floor().to(torch.int32)
+    assert_parity(pkg, workloads().custom(sl.tolist(), seed=82))
+
+
 @pytest.mark.parametrize("cfg", [1, 3])
 def test_cluster_kernel_path(pkg, cfg, monkeypatch):
     """The one-launch cluster kernel (used when no workspace can be had, and
