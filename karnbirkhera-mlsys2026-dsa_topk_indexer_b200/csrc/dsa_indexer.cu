@@ -280,11 +280,10 @@ bool side_stream(cudaStream_t stream, cudaStream_t* side, cudaEvent_t* fork, cud
 // Tensor maps over the caller's buffers (encoded per call: they hold the
 // base address).
 int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_pages, CUtensorMap* tk,
-              CUtensorMap* ts, CUtensorMap* tq) {
+              CUtensorMap* tq) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return DSA_ERR_CUDA;
   std::memset(tk, 0, sizeof(*tk));
-  std::memset(ts, 0, sizeof(*ts));
   std::memset(tq, 0, sizeof(*tq));
   const cuuint32_t estr[3] = {1, 1, 1};
   {  // page data: {128 bytes, 64 tokens, num_pages}, box = one page, 128-byte swizzle
@@ -294,16 +293,6 @@ int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_page
     const cuuint32_t box[3] = {static_cast<cuuint32_t>(kDim), static_cast<cuuint32_t>(kPage), 1};
     if (enc(tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(kcache), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return DSA_ERR_CUDA;
-  }
-  {  // page scales: {64 fp32, num_pages} starting at byte 8192 of page 0
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kPage), static_cast<cuuint64_t>(num_pages)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kPageBytes)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kPage), 1};
-    void* base = const_cast<uint8_t*>(static_cast<const uint8_t*>(kcache) + kPageData);
-    if (enc(ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return DSA_ERR_CUDA;
   }
@@ -319,11 +308,13 @@ int make_maps(const void* q, const void* kcache, int64_t batch, int64_t num_page
   return DSA_OK;
 }
 
-// CTAs per request (the cluster size). Enough CTAs to give the GPU about four
-// per SM in total, so short batches split their rows widely (latency) while
-// large batches keep whole rows on few CTAs (less merging per byte); never
-// fewer than about 4 tiles per CTA. Measured on B200: B=64 -> 8 (best of
-// 2/4/8), B=512 -> 2 (best of 1/2/4/8).
+// CTAs per request (the cluster size). About four CTAs per SM in total, so
+// short batches split their rows widely (latency) while large batches keep
+// whole rows on few CTAs (less merging per byte); rounded down above 2 (one
+// fewer cluster wave beats one more CTA per row); never fewer than about 4
+// tiles per CTA. Measured on B200 (config 2 rows): B=64 -> 8 (best of
+// 4/6/7/8/16), B=128 -> 4 (best of 3/4/5/6), B=256 -> 2 (2 and 3 equal),
+// B=512 -> 2 (best of 1/2/4/8). 16-CTA clusters lost everywhere.
 int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
   // DSA_TOPK_CLUSTER=<1..16> overrides the choice (tuning and tests; sizes
   // above 8 are a non-portable cluster size B200 supports).
@@ -333,6 +324,7 @@ int choose_cluster(int64_t batch, int64_t span_pages, int num_sms) {
   }
   const int64_t tiles = (span_pages + 1) / 2;
   int64_t g = (4 * static_cast<int64_t>(num_sms) + batch - 1) / batch;
+  if (g > 2) g = (4 * static_cast<int64_t>(num_sms)) / batch;
   const int64_t g_floor = (tiles + 3) / 4;
   if (g > g_floor) g = g_floor;
   if (g < 1) g = 1;
@@ -367,8 +359,8 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   int num_sms = 0;
   int rc = prepare_device(&num_sms);
   if (rc != DSA_OK) return rc;
-  CUtensorMap tk, ts, tq;
-  rc = make_maps(q, kcache, prm.batch, prm.num_pages, &tk, &ts, &tq);
+  CUtensorMap tk, tq;
+  rc = make_maps(q, kcache, prm.batch, prm.num_pages, &tk, &tq);
   if (rc != DSA_OK) return rc;
   const int G = choose_cluster(prm.batch, span_pages, num_sms);
   IndexerParams params = prm;
@@ -376,7 +368,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
   auto launch = [&](const IndexerParams& pp, int64_t rows, int g, cudaStream_t st) -> int {
     // Two-class launches with in-kernel ranking use the instantiation that
     // decides the split on the device.
-    void (*kern)(CUtensorMap, CUtensorMap, CUtensorMap, IndexerParams) = indexer_kernel<kMode>;
+    void (*kern)(CUtensorMap, CUtensorMap, IndexerParams) = indexer_kernel<kMode>;
     if constexpr (kMode != kModeScores) {
       if (pp.split_role >= 0) kern = indexer_kernel<kMode, true>;
     }
@@ -392,7 +384,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tk, ts, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+    return cudaLaunchKernelEx(&cfg, kern, tk, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
   };
 
   // Shared-sequence stage (DSA_TOPK_PREFILL=1): plan (row order + group
@@ -413,7 +405,7 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
       if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
       PrefillParams pp{group_order, handled};
       KernelTimer timer(stream);
-      prefill_kernel<kMode><<<static_cast<unsigned>(ngroups), kPThreads, kPSmemBytes, stream>>>(tk, ts, tq, prm, pp);
+      prefill_kernel<kMode><<<static_cast<unsigned>(ngroups), kPThreads, kPSmemBytes, stream>>>(tk, tq, prm, pp);
       if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
       params.order = order;
       params.order_base = -1;
@@ -504,9 +496,10 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
 std::atomic<int> g_test_skip_tile{-1};
 std::atomic<uint64_t> g_test_wait_ns{ptx::kWaitTimeoutNs};
 
-IndexerParams base_params(const float* w, const int32_t* sl, const int32_t* bt, int64_t batch, int64_t max_pages,
-                          int64_t num_pages) {
+IndexerParams base_params(const void* kcache, const float* w, const int32_t* sl, const int32_t* bt, int64_t batch,
+                          int64_t max_pages, int64_t num_pages) {
   IndexerParams p{};
+  p.kcache = static_cast<const uint8_t*>(kcache);
   p.skip_tile = g_test_skip_tile.load();
   p.wait_ns = g_test_wait_ns.load();
   p.seq_lens = sl;
@@ -531,7 +524,7 @@ extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!topk_indices) return DSA_ERR_INVALID_ARG;
-  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  IndexerParams p = base_params(k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
   return launch_indexer<kModeTopK>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
 }
@@ -552,7 +545,7 @@ extern "C" int dsa_topk_indexer_scores(const void* q, const void* k_cache, const
   fill_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       scores, n, -__builtin_huge_valf());
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
-  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  IndexerParams p = base_params(k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.scores = scores;
   p.score_stride = score_stride;
   rc = launch_indexer<kModeScores>(q, k_cache, p, max_pages, static_cast<cudaStream_t>(stream));
@@ -569,7 +562,7 @@ extern "C" int dsa_topk_indexer_partial(const void* q, const void* k_cache, cons
   int rc = check_common(q, k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   if (rc != DSA_OK || batch == 0) return rc;
   if (!cand_scores || !cand_pos || key_begin < 0 || key_end < key_begin) return DSA_ERR_INVALID_ARG;
-  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  IndexerParams p = base_params(k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.cand_scores = cand_scores;
   p.cand_pos = cand_pos;
   p.key_begin = key_begin;
@@ -642,11 +635,11 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
   int32_t* order = nullptr;
   rc = noalloc_scratch(&order);
   if (rc != DSA_OK) return rc;
-  CUtensorMap tk, ts, tq;
-  rc = make_maps(q, k_cache, batch, num_pages, &tk, &ts, &tq);
+  CUtensorMap tk, tq;
+  rc = make_maps(q, k_cache, batch, num_pages, &tk, &tq);
   if (rc != DSA_OK) return rc;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  IndexerParams p = base_params(weights, seq_lens, block_table, batch, max_pages, num_pages);
+  IndexerParams p = base_params(k_cache, weights, seq_lens, block_table, batch, max_pages, num_pages);
   p.out = topk_indices;
   const int G = choose_cluster(batch, max_pages, num_sms);
   int launches = 1;
@@ -675,7 +668,7 @@ extern "C" int dsa_topk_indexer_launch_noalloc(const void* q, const void* k_cach
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   KernelTimer timer(st);
-  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kModeTopK>, tk, ts, tq, p) != cudaSuccess) return DSA_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, indexer_kernel<kModeTopK>, tk, tq, p) != cudaSuccess) return DSA_ERR_CUDA;
   timer.stop();
   t_last_launches = launches;
   t_last_path = "noalloc";

@@ -56,8 +56,7 @@ constexpr int kBarLow = 2;   // threads 0..255 (final ordering in CTA 0)
 // Shared memory map (byte offsets from a 1024-aligned base).
 constexpr int kOffK = 0;                                  // kStages x 16384, swizzled K tiles
 constexpr int kOffQ = kOffK + kStages * 16384;            // 8192, swizzled Q
-constexpr int kOffScale = kOffQ + 8192;                   // kStages x 512 (128 fp32)
-constexpr int kOffCand = kOffScale + kStages * 512;       // kCap x 8
+constexpr int kOffCand = kOffQ + 8192;                    // kCap x 8
 constexpr int kOffHist = kOffCand + kCap * 8;             // 2 x 256 x 4
 constexpr int kOffTot = kOffHist + 2 * 256 * 4;           // 256 x 4
 constexpr int kOffW = kOffTot + 256 * 4;                  // 64 x 4
@@ -99,6 +98,7 @@ enum MiscWord : int {
 };
 
 struct IndexerParams {
+  const uint8_t* kcache;       // page pool (the epilogue reads the key scales from it)
   const int32_t* order;        // [B] request served by cluster c (longest first), or null
   const int32_t* seq_lens;     // [B]
   const int32_t* block_table;  // [B, max_pages]
@@ -135,44 +135,64 @@ struct IndexerParams {
 };
 
 constexpr int kInKernelOrderMax = 256;  // rows ranked in-kernel at most
-static_assert(kCap * 8 >= kInKernelOrderMax * 8, "in-kernel row ranking scratch (candidate buffer)");
+static_assert(kCap * 8 >= kInKernelOrderMax * 12, "in-kernel row ranking scratch (candidate buffer)");
 
 // Longest-first rank -> row, computed by every CTA from the clamped lengths
 // (ties: smaller row first, as the plan kernel's counting sort would give
-// within a bucket). All kThreads threads; `scratch` holds 2 x batch ints.
-// kTwoClass: it also decides the two-class launch (*split = 1 if the split
-// pays, split_beats_waves).
+// within a bucket). All kThreads threads; `scratch` holds 3 x
+// kInKernelOrderMax words; *total is 64-bit scratch. kTwoClass: it also
+// decides the two-class launch (*split = 1 if the split pays,
+// split_beats_waves).
 __device__ __forceinline__ bool split_beats_waves(const IndexerParams& p, const int32_t* sorted_tiles, int64_t total);
 
 template <bool kTwoClass>
 __device__ __forceinline__ int row_of_rank(const IndexerParams& p, int target, int32_t* scratch, uint32_t* result,
-                                           uint32_t* split) {
+                                           uint32_t* split, unsigned long long* total) {
+  // Row j's key (tiles << 32 | ~j) is unique and orders the rows longest
+  // first, ties by row: the rank of row i is the number of larger keys,
+  // counted by thread i over all keys two at a time (broadcast loads).
   const int64_t cap = static_cast<int64_t>(p.max_pages) * kPage;
-  int32_t* sorted_tiles = scratch + p.batch;
-  for (int j = threadIdx.x; j < p.batch; j += kThreads) {
-    int64_t l = p.seq_lens[j];
-    l = l < 0 ? 0 : (l > cap ? cap : l);
-    scratch[j] = static_cast<int32_t>((l + 2 * kPage - 1) / (2 * kPage));  // tiles
+  const int B = p.batch;
+  const int Bp = (B + 1) & ~1;  // padded with key 0, below every row's key
+  uint64_t* key = reinterpret_cast<uint64_t*>(scratch);
+  int32_t* sorted_tiles = scratch + 2 * kInKernelOrderMax;
+  for (int j = threadIdx.x; j < Bp; j += kThreads) {
+    uint64_t k = 0ull;
+    if (j < B) {
+      int64_t l = p.seq_lens[j];
+      l = l < 0 ? 0 : (l > cap ? cap : l);
+      const uint64_t t = static_cast<uint64_t>((l + 2 * kPage - 1) / (2 * kPage));  // tiles
+      k = (t << 32) | static_cast<uint64_t>(0xFFFFFFFFu - static_cast<uint32_t>(j));
+    }
+    key[j] = k;
   }
-  if (threadIdx.x == 0) *result = 0u;
+  if (threadIdx.x == 0) {
+    *result = 0u;
+    if constexpr (kTwoClass) *total = 0ull;
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < p.batch; i += kThreads) {
-    const int32_t li = scratch[i];
+  const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(key);
+  for (int i = threadIdx.x; i < B; i += kThreads) {
+    const uint64_t ki = key[i];
     int r = 0;
-    for (int j = 0; j < p.batch; ++j) {
-      const int32_t lj = scratch[j];
-      r += (lj > li || (lj == li && j < i)) ? 1 : 0;
+#pragma unroll 8
+    for (int q = 0; q < Bp / 2; ++q) {
+      const ulonglong2 v = k2[q];
+      r += (v.x > ki ? 1 : 0) + (v.y > ki ? 1 : 0);
     }
     if (r == target) *result = static_cast<uint32_t>(i);
-    if constexpr (kTwoClass) sorted_tiles[r] = li;
+    if constexpr (kTwoClass) sorted_tiles[r] = static_cast<int32_t>(ki >> 32);
+  }
+  if constexpr (kTwoClass) {  // total tiles: warp sums, one shared atomic per warp
+    unsigned long long sum = 0ull;
+    for (int j = threadIdx.x; j < B; j += kThreads) sum += key[j] >> 32;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, off);
+    if ((threadIdx.x & 31) == 0 && sum) atomicAdd(total, sum);
   }
   __syncthreads();
   if constexpr (kTwoClass) {
-    if (threadIdx.x == 0) {
-      int64_t total = 0;
-      for (int j = 0; j < p.batch; ++j) total += scratch[j];
-      *split = split_beats_waves(p, sorted_tiles, total) ? 1u : 0u;
-    }
+    if (threadIdx.x == 0) *split = split_beats_waves(p, sorted_tiles, static_cast<int64_t>(*total)) ? 1u : 0u;
     __syncthreads();
   }
   return static_cast<int>(*result);
@@ -447,8 +467,8 @@ __device__ __forceinline__ void cluster_select_emit(uint8_t* smem, uint32_t base
 // so that the single-launch kernel carries none of it.
 template <int kMode, bool kTwoClass = false>
 __global__ void __launch_bounds__(kThreads, 2)
-    indexer_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
-                   const __grid_constant__ CUtensorMap tm_q, const IndexerParams p) {
+    indexer_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                   const IndexerParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_addr(smem_raw);
   const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
@@ -475,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b = p.order_base >= 0
                     ? row_of_rank<kTwoClass>(p, p.order_base + static_cast<int>(blockIdx.x / G),
                                              reinterpret_cast<int32_t*>(smem + kOffCand), misc_nv + kMiscSel,
-                                             misc_nv + kMiscSel + 1)
+                                             misc_nv + kMiscSel + 1, mm)
                     : (p.order ? p.order[blockIdx.x / G] : static_cast<int>(blockIdx.x / G));
   if (p.handled && p.handled[b]) return;  // uniform over the cluster, before any barrier or TMEM use
   if constexpr (kTwoClass) {  // does this launch serve this rank? (uniform over the cluster)
@@ -508,11 +528,41 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int pg_end = (page_lo + 2 * t1 < page_hi) ? page_lo + 2 * t1 : page_hi;
   const int32_t* bt_row = p.block_table + static_cast<int64_t>(b) * p.max_pages;
 
+  // ---- key scales (epilogue) ----
+  // Key scales come straight from the page pool with global loads issued
+  // two tiles of the epilogue group ahead (their page ids one tile ahead of
+  // that), so the epilogue never waits for or releases a K ring stage: the
+  // MMA commit alone frees a stage. The first loads are issued before the
+  // setup below, which hides their latency. Epilogue warp (group g, lane
+  // quarter q) scores key row 32q + lane of the group's tiles; its 32 keys
+  // lie in one page of the tile (quarters 0-1: the first page, 2-3: the
+  // second).
+  const int epi_q4 = warp & 3;
+  const int epi_row = epi_q4 * 32 + lane;
+  const int epi_grp = (warp - 2) >> 2;
+  const uint8_t* scale_base = p.kcache + kPageData + 4 * (epi_row & (kPage - 1));
+  auto page_of = [&](int t) -> int32_t {  // warp-uniform; -1: no page
+    const int pi = pg_first + 2 * t + (epi_q4 >> 1);
+    return (t < my_tiles && pi < pg_end) ? __ldg(bt_row + pi) : -1;
+  };
+  auto scale_of = [&](int32_t pid) -> float {  // out-of-range ids read nothing (TMA zero-fills their keys)
+    return static_cast<uint64_t>(static_cast<uint32_t>(pid)) < static_cast<uint64_t>(p.num_pages)
+               ? __ldg(reinterpret_cast<const float*>(scale_base + static_cast<int64_t>(pid) * kPageBytes))
+               : 0.f;
+  };
+  float sc_next = 0.f, sc_after = 0.f;  // scales of the group's tiles i and i + 2
+  int32_t pid_ahead = -1;               // page id for tile i + 4
+  if (warp >= 2) {
+    sc_next = scale_of(page_of(epi_grp));
+    sc_after = scale_of(page_of(epi_grp + 2));
+    pid_ahead = page_of(epi_grp + 4);
+  }
+
   // ---- setup ----
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, 1 + 4);  // MMA commit + the 4 warps of one epilogue group
+      ptx::mbar_init(bar_empty + 8 * s, 1);  // the MMA commit: the epilogue never reads the K ring
     }
     for (int i = 0; i < kTmemBufs; ++i) {
       ptx::mbar_init(bar_tfull + 8 * i, 1);
@@ -525,7 +575,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     misc_nv[kMiscRot] = misc_nv[kMiscRot + 1] = misc_nv[kMiscRot + 2] = 0u;
     misc_nv[kMiscNBase] = misc_nv[kMiscSlot] = 0u;
     ptx::prefetch_tmap(&tm_k);
-    ptx::prefetch_tmap(&tm_s);
     ptx::prefetch_tmap(&tm_q);
   }
   if (warp == 1) {
@@ -577,17 +626,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (static_cast<uint64_t>(static_cast<uint32_t>(pa)) >= static_cast<uint64_t>(p.num_pages) ||
             (has_b && static_cast<uint64_t>(static_cast<uint32_t>(pb)) >= static_cast<uint64_t>(p.num_pages)))
           atomicOr(&g_dsa_status, DSA_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range boxes
-        const uint32_t bytes = has_b ? 2u * (kPageData + 256u) : (kPageData + 256u);
+        const uint32_t bytes = has_b ? 2u * kPageData : kPageData;
         const uint32_t fb = bar_full + 8 * s;
         const uint32_t kdst = base_addr + kOffK + s * 16384;
-        const uint32_t sdst = base_addr + kOffScale + s * 512;
         ptx::mbar_arrive_expect_tx(fb, bytes);
         ptx::tma_load_3d(kdst, &tm_k, fb, 0, 0, pa, pol_stream);
-        ptx::tma_load_2d(sdst, &tm_s, fb, 0, pa, pol_stream);
-        if (has_b) {
-          ptx::tma_load_3d(kdst + kPageData, &tm_k, fb, 0, 0, pb, pol_stream);
-          ptx::tma_load_2d(sdst + 256, &tm_s, fb, 0, pb, pol_stream);
-        }
+        if (has_b) ptx::tma_load_3d(kdst + kPageData, &tm_k, fb, 0, 0, pb, pol_stream);
       }
       __syncwarp();
       issued = i + 1;
@@ -661,29 +705,16 @@ __global__ void __launch_bounds__(kThreads, 2)
     // loop early would strand the other group at a named barrier.
 #pragma unroll 1
     for (int i = grp; i < my_tiles; i += 2) {
-      const int s = i % kStages;
-      const uint32_t ph = static_cast<uint32_t>(i / kStages) & 1u;
       float score = 0.f;
-      if (!aborted) {
-        const bool ok =
-            ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
-        if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
-      }
+      const float scale = sc_next;
+      sc_next = sc_after;
+      sc_after = scale_of(pid_ahead);  // tile i + 4
+      pid_ahead = page_of(i + 6);
       const int buf = i % kTmemBufs;
       if (!aborted) {
-        // The scale is read with a generic-proxy load, and the producer's next
-        // TMA into this stage writes through the async proxy as soon as the MMA
-        // commit and this group's four warps have arrived. Without the proxy
-        // fence that write-after-read is unordered: on L2-resident pages the
-        // refill landed first and the key was scaled by the scale of the tile
-        // four steps ahead.
-        const float scale = ptx::lds_f32_ordered(base_addr + kOffScale + 4u * (s * kTileKeys + row));
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
         const uint32_t bph = static_cast<uint32_t>(i / kTmemBufs) & 1u;
-        const bool ok =
-            ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
+        const bool ok = ptx::mbar_wait(bar_tfull + 8 * buf, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
+                                       p.wait_ns);
         if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
         if (!aborted) {
           __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged

@@ -5,21 +5,22 @@
 //
 // One CTA per SM (18 warps, 512 TMEM columns):
 //   warp 0      TMA producer: the four query boxes once, then per tile two
-//               8 KB page boxes and two 256 B scale rows into a 4-stage ring;
+//               8 KB page boxes into a 4-stage ring (freed by the MMA);
 //   warp 1      TMEM owner and MMA issuer: D[128 keys x 256] (fp32 in TMEM,
 //               one buffer per tile parity) = K_tile[128 x 128 e4m3] .
 //               Q[256 x 128 e4m3]^T as four tcgen05.mma kind::f8f6f4 (K = 32);
 //   warps 2..17 sixteen epilogue warps: warp (parity, pair, quarter) takes the
 //               tiles of one parity, the two rows of one pair, and the 32 keys
-//               of one TMEM lane quarter (thread = key). Per tile it waits,
-//               reads the key scales and releases the stage once, then scores
+//               of one TMEM lane quarter (thread = key). Per tile it waits
+//               for the accumulators once (key scales come from the page
+//               pool with global loads issued two tiles ahead), then scores
 //               both rows from their 64 head columns (relu / head weight /
 //               scale in registers) and appends the keys above each row's
 //               threshold to that row's candidate buffer, cut to the best
 //               2048 when nearly full. The eight warps of a pair (both
 //               parities) meet only at those checks.
-// Scoring two rows per warp shares every per-tile wait, stage release and
-// TMEM hand-off between them; the math itself (64 max + 32 packed FMA per key
+// Scoring two rows per warp shares every per-tile wait and TMEM hand-off
+// between them; the math itself (64 max + 32 packed FMA per key
 // and row) is what bounds the kernel.
 // After the stream each pair's 256 threads take its two rows in turn: exact
 // radix select down to 2048 when more remain, then the bucket ordering and
@@ -53,8 +54,7 @@ constexpr int kPTmemCols = 2 * kPBufCols;          // two buffers: all 512 colum
 // Shared memory map (byte offsets from a 1024-aligned base).
 constexpr int kPOffK = 0;                                  // kPStages x 16384, swizzled K tiles
 constexpr int kPOffQ = kPOffK + kPStages * 16384;          // kPQ x 8192, swizzled Q (N = 256 rows)
-constexpr int kPOffScale = kPOffQ + kPQ * 8192;            // kPStages x 512
-constexpr int kPOffCand = kPOffScale + kPStages * 512;     // kPQ x kPCap x 8
+constexpr int kPOffCand = kPOffQ + kPQ * 8192;             // kPQ x kPCap x 8
 constexpr int kPOffHist = kPOffCand + kPQ * kPCap * 8;     // kPQ x 256 x 4
 constexpr int kPOffW = kPOffHist + kPQ * 256 * 4;          // kPQ x 64 x 4
 constexpr int kPOffBar = kPOffW + kPQ * kHeads * 4;        // 256
@@ -66,7 +66,7 @@ static_assert((2 * kPStages + 2 * 2 + 1) * 8 <= 256, "barrier area");
 // After the stream the K ring and Q area hold the ordering scratch of the two
 // pairs: tmp 2048 x 8, bucket ids 2048 x 2, three 2048-word count arrays.
 constexpr int kPRankBytes = kTopK * 8 + kTopK * 2 + 3 * 2048 * 4;
-static_assert(2 * kPRankBytes <= kPOffScale, "ordering scratch of both pairs fits in the K ring and Q area");
+static_assert(2 * kPRankBytes <= kPOffCand, "ordering scratch of both pairs fits in the K ring and Q area");
 static_assert(kPRankBytes % 16 == 0, "16-byte aligned scratch");
 
 // Per-row misc words (uint32 at kPOffMisc + 128 * j).
@@ -95,8 +95,8 @@ struct PrefillParams {
 // 96 registers per thread is the ceiling.
 template <int kMode>
 __global__ void __launch_bounds__(kPThreads, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_s,
-                   const __grid_constant__ CUtensorMap tm_q, const IndexerParams p, const PrefillParams pp) {
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_q,
+                   const IndexerParams p, const PrefillParams pp) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_addr(smem_raw);
   const uint32_t base_addr = (raw_addr + 1023u) & ~1023u;
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, 1 + 8);  // MMA commit + the 8 warps of the tile's parity
+      ptx::mbar_init(bar_empty + 8 * s, 1);  // the MMA commit: the epilogue never reads the K ring
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(bar_tfull + 8 * i, 1);
@@ -184,7 +184,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
     ptx::fence_mbar_init();
     shared_misc[kPAbort] = 0u;
     ptx::prefetch_tmap(&tm_k);
-    ptx::prefetch_tmap(&tm_s);
     ptx::prefetch_tmap(&tm_q);
   }
   if (threadIdx.x < kPQ * 32) {  // misc words of the four rows
@@ -246,17 +245,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (static_cast<uint64_t>(static_cast<uint32_t>(pa)) >= static_cast<uint64_t>(p.num_pages) ||
             (has_b && static_cast<uint64_t>(static_cast<uint32_t>(pb)) >= static_cast<uint64_t>(p.num_pages)))
           atomicOr(&g_dsa_status, DSA_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range boxes
-        const uint32_t bytes = has_b ? 2u * (kPageData + 256u) : (kPageData + 256u);
+        const uint32_t bytes = has_b ? 2u * kPageData : kPageData;
         const uint32_t fb = bar_full + 8 * s;
         const uint32_t kdst = base_addr + kPOffK + s * 16384;
-        const uint32_t sdst = base_addr + kPOffScale + s * 512;
         ptx::mbar_arrive_expect_tx(fb, bytes);
         ptx::tma_load_3d(kdst, &tm_k, fb, 0, 0, pa, pol_stream);
-        ptx::tma_load_2d(sdst, &tm_s, fb, 0, pa, pol_stream);
-        if (has_b) {
-          ptx::tma_load_3d(kdst + kPageData, &tm_k, fb, 0, 0, pb, pol_stream);
-          ptx::tma_load_2d(sdst + 256, &tm_s, fb, 0, pb, pol_stream);
-        }
+        if (has_b) ptx::tma_load_3d(kdst + kPageData, &tm_k, fb, 0, 0, pb, pol_stream);
       }
       __syncwarp();
       issued = i + 1;
@@ -317,6 +311,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const uint32_t hi_A = static_cast<uint32_t>(row_hi(jA)), hi_B = static_cast<uint32_t>(row_hi(jB));
     const uint32_t lo32 = static_cast<uint32_t>(lo);
     const int n_pairs_full = n_tiles >> 1;
+    // Key scales straight from the page pool, two tiles of the parity ahead
+    // (page ids one tile ahead of that), as in the per-row kernel: the
+    // epilogue never waits for or releases a K ring stage.
+    const uint8_t* scale_base = p.kcache + kPageData + 4 * (row & (kPage - 1));
+    auto page_of = [&](int t) -> int32_t {  // warp-uniform; -1: no page
+      const int pi = page_lo + 2 * t + (q4 >> 1);
+      return (t < n_tiles && pi < page_hi) ? __ldg(bt_ref + pi) : -1;
+    };
+    auto scale_of = [&](int32_t pid) -> float {
+      return static_cast<uint64_t>(static_cast<uint32_t>(pid)) < static_cast<uint64_t>(p.num_pages)
+                 ? __ldg(reinterpret_cast<const float*>(scale_base + static_cast<int64_t>(pid) * kPageBytes))
+                 : 0.f;
+    };
+    float sc_next = scale_of(page_of(par)), sc_after = scale_of(page_of(par + 2));
+    int32_t pid_ahead = page_of(par + 4);
     uint64_t thr_A = 0, thr_B = 0;  // keys below thr can no longer reach the row's top 2048
     uint32_t nb_A = 0, nb_B = 0;    // candidates counted at the last check
     uint32_t slot = 0;              // rotating append counter of the current interval (both rows)
@@ -369,24 +378,15 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // still meets its pair at every check barrier.
 #pragma unroll 1
     for (int i = par; i < n_tiles; i += 2) {
-      const int s = i % kPStages;
-      const uint32_t ph = static_cast<uint32_t>(i / kPStages) & 1u;
+      const float scale = sc_next;
+      sc_next = sc_after;
+      sc_after = scale_of(pid_ahead);  // tile i + 4
+      pid_ahead = page_of(i + 6);
       const uint32_t tile_key0 = static_cast<uint32_t>(page_lo + 2 * i) * kPage;
       const bool live_A = tile_key0 < hi_A && tile_key0 + kTileKeys > lo32;  // the tile holds keys of row A
       const bool live_B = tile_key0 < hi_B && tile_key0 + kTileKeys > lo32;
       float sc_A = 0.f, sc_B = 0.f;
       if (!aborted) {
-        const bool ok =
-            ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
-        if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
-      }
-      if (!aborted) {
-        // Generic-proxy read of the scale, then the proxy fence before the
-        // stage is released to the next TMA write (see indexer_kernel).
-        const float scale = ptx::lds_f32_ordered(base_addr + kPOffScale + 4u * (s * kTileKeys + row));
-        ptx::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
         const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
         const bool ok = ptx::mbar_wait(bar_tfull + 8 * par, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
                                        p.wait_ns);

@@ -253,11 +253,13 @@ def test_seq_len_clamped_flags_status(pkg):
     assert (out[0, :1024] >= 0).all() and (out[0, 1024:] == -1).all()
 
 
-@pytest.mark.parametrize("g", [1, 2, 3, 8])
+@pytest.mark.parametrize("g", [1, 2, 3, 5, 8, 16])
 def test_forced_cluster_sizes_l2_resident(pkg, g, monkeypatch):
-    """Every cluster size on a shared, L2-resident K (an epilogue-bound
-    pipeline where ring stages are refilled fastest): rows of 9-70 tiles per
-    CTA, so every ring stage is reused several times."""
+    """Cluster sizes 1 to 16 on a shared, L2-resident K (an epilogue-bound
+    pipeline where ring stages are refilled fastest): rows of 71 tiles, so up
+    to 8 CTAs per row reuse every ring stage; the cluster-wide ordering ranks
+    each CTA's survivors against every other CTA's bucket table (16: the
+    largest cluster, a non-portable size)."""
     monkeypatch.setenv("DSA_TOPK_CLUSTER", str(g))
     w = workloads().make_shared("l2res", 192, 9000, 160, 21)
     assert_parity(pkg, _rows(w, list(range(0, 192, 3))))
