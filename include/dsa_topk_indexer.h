@@ -201,8 +201,9 @@ DSA_API int dsa_topk_indexer_last_launch_count(void);
 
 /* Schedule the last successful top-K call on this host thread took:
  * "cluster" (one cluster kernel, optionally after the longest-first plan),
- * "cluster-split" (two concurrent cluster kernels) or "noalloc" (the
- * no-allocation entry point's cluster kernel). */
+ * "cluster-split" (two concurrent cluster kernels), "prefill+cluster" (the
+ * shared-sequence kernel, then the cluster kernel for the rows it left) or
+ * "noalloc" (the no-allocation entry point's cluster kernel). */
 DSA_API const char* dsa_topk_indexer_last_path(void);
 
 /* Per-kernel timing for profiling, off by default. While on, every call

@@ -343,15 +343,17 @@ int check_common(const void* q, const void* kcache, const float* w, const int32_
   return DSA_OK;
 }
 
-// With DSA_TOPK_PREFILL=1, batches of at least this many rows first go
-// through the shared-sequence kernel (prefill_kernel), which serves every
-// group of four consecutive rows that read the same pages (causal prefill
-// rows of one sequence) and leaves the others to the per-row kernel. It is
-// off by default: measured on B200 it matches the per-row kernel on the
-// 8192-row causal prefill (0.95 ms) and trails it on the 2048-row long
-// context (4.39 vs 4.23 ms: 512 groups fill 3.46 waves of 148 SMs), while
-// its extra launches add ~14 us to a 512-row decode batch.
+// Batches of at least kPrefillMinRows rows whose block table must share
+// pages (more entries than kPrefillShareFactor times the pool holds pages:
+// causal prefill rows of one sequence) first go through the shared-sequence
+// kernel (prefill_kernel), which serves every group of four consecutive rows
+// that really read the same pages and leaves the others to the per-row
+// kernel. Measured on B200: 8192-row causal prefill 0.913 vs 0.951 ms,
+// 2048-row long context 4.00 vs 4.07 ms. Decode batches (distinct pages per
+// row) never take it: its launches would add ~10 us for nothing.
+// DSA_TOPK_PREFILL=0 turns it off, =1 tries it on any batch of 256+ rows.
 constexpr int64_t kPrefillMinRows = 256;
+constexpr int64_t kPrefillShareFactor = 4;
 
 template <int kMode>
 int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, int64_t span_pages,
@@ -387,16 +389,18 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     return cudaLaunchKernelEx(&cfg, kern, tk, tq, pp) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
   };
 
-  // Shared-sequence stage (DSA_TOPK_PREFILL=1): plan (row order + group
-  // order), then the prefill kernel over the groups, longest first; the
-  // per-row kernel below skips the rows it served.
+  // Shared-sequence stage: plan (row order + group order), then the prefill
+  // kernel over the groups, longest first; the per-row kernel below skips
+  // the rows it served.
   if constexpr (kMode != kModeScores) {
     const char* env = std::getenv("DSA_TOPK_PREFILL");
     const int64_t B = prm.batch;
     const int64_t ngroups = (B + kGroupRows - 1) / kGroupRows;
-    uint8_t* ws = (B < kPrefillMinRows || !(env && env[0] == '1'))
-                      ? nullptr
-                      : static_cast<uint8_t*>(workspace(stream, static_cast<size_t>(8 * B + 4 * ngroups)));
+    bool shared = B >= kPrefillMinRows && B * static_cast<int64_t>(prm.max_pages) > kPrefillShareFactor * prm.num_pages;
+    if (env && env[0] == '0') shared = false;
+    if (env && env[0] == '1') shared = B >= kPrefillMinRows;
+    uint8_t* ws = shared ? static_cast<uint8_t*>(workspace(stream, static_cast<size_t>(8 * B + 4 * ngroups)))
+                         : nullptr;
     if (ws) {
       int32_t* order = reinterpret_cast<int32_t*>(ws);
       int32_t* handled = order + B;

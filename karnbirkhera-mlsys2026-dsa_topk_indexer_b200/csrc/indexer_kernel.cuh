@@ -42,7 +42,7 @@ constexpr int kTileKeys = 128;
 constexpr int kStages = 4;
 constexpr int kThreads = 320;     // 10 warps
 constexpr int kEpiThreads = 256;  // warps 2..9
-constexpr int kCap = 4096;        // candidate keys per CTA
+constexpr int kCap = 4608;        // candidate keys per CTA (the rest of half an SM)
 constexpr int kSoloCap = 3072;    // candidates a one-CTA row ranks at once (12 per thread)
 constexpr int kTmemBufs = 4;
 constexpr int kTmemCols = kTmemBufs * kHeads;

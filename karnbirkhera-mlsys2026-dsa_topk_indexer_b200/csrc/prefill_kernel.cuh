@@ -1,14 +1,18 @@
 // Shared-sequence indexer kernel (prefill): one CTA serves four consecutive
 // query rows that read the same pages (the causal rows of one sequence share
-// its block-table row), so every K tile is loaded once and feeds one
-// tcgen05.mma with N = 4 queries x 64 heads = 256.
+// its block-table row), so every K tile is loaded once and feeds the MMAs of
+// all four rows.
 //
-// One CTA per SM (18 warps, 512 TMEM columns):
+// One CTA per SM (19 warps, 512 TMEM columns):
 //   warp 0      TMA producer: the four query boxes once, then per tile two
-//               8 KB page boxes into a 4-stage ring (freed by the MMA);
-//   warp 1      TMEM owner and MMA issuer: D[128 keys x 256] (fp32 in TMEM,
-//               one buffer per tile parity) = K_tile[128 x 128 e4m3] .
-//               Q[256 x 128 e4m3]^T as four tcgen05.mma kind::f8f6f4 (K = 32);
+//               8 KB page boxes into a 4-stage ring (freed when both MMA
+//               issuers have committed);
+//   warps 1, 18 MMA issuers, one per row pair (warp 1 also owns TMEM):
+//               D[128 keys x 128] (fp32 in TMEM, one buffer per tile parity
+//               and pair) = K_tile[128 x 128 e4m3] . Q_pair[128 x 128 e4m3]^T
+//               as four tcgen05.mma kind::f8f6f4 (K = 32). A pair whose
+//               epilogue is busy (a candidate-buffer cut) holds up only its
+//               own issuer;
 //   warps 2..17 sixteen epilogue warps: warp (parity, pair, quarter) takes the
 //               tiles of one parity, the two rows of one pair, and the 32 keys
 //               of one TMEM lane quarter (thread = key). Per tile it waits
@@ -45,11 +49,12 @@ namespace dsa {
 
 constexpr int kPQ = kGroupRows;                    // query rows per CTA (4)
 constexpr int kPStages = 4;                        // K ring stages
-constexpr int kPWarps = 2 + 16;                    // producer, MMA, 16 epilogue warps
-constexpr int kPThreads = 32 * kPWarps;            // 576
-constexpr int kPCap = 3584;                        // candidate keys per row
-constexpr int kPBufCols = kPQ * kHeads;            // TMEM columns of one tile (N = 256)
-constexpr int kPTmemCols = 2 * kPBufCols;          // two buffers: all 512 columns
+constexpr int kPWarps = 3 + 16;                    // producer, two MMA issuers, 16 epilogue warps
+constexpr int kPThreads = 32 * kPWarps;            // 608
+constexpr int kPMmaWarp1 = 18;                     // MMA issuer of row pair 1 (warp 1: pair 0)
+constexpr int kPCap = 3968;                        // candidate keys per row (the rest of the 227 KB)
+constexpr int kPBufCols = 2 * kHeads;              // TMEM columns of one row pair's tile (N = 128)
+constexpr int kPTmemCols = 4 * kPBufCols;          // (parity, pair) buffers: all 512 columns
 
 // Shared memory map (byte offsets from a 1024-aligned base).
 constexpr int kPOffK = 0;                                  // kPStages x 16384, swizzled K tiles
@@ -62,7 +67,7 @@ constexpr int kPOffMisc = kPOffBar + 256;                  // kPQ x 128 per row 
 constexpr int kPSmemUsed = kPOffMisc + kPQ * 128 + 128;
 constexpr int kPSmemBytes = kPSmemUsed + 1024;             // alignment slack
 static_assert(kPSmemBytes <= 232448, "one CTA per SM");
-static_assert((2 * kPStages + 2 * 2 + 1) * 8 <= 256, "barrier area");
+static_assert((2 * kPStages + 2 * 4 + 1) * 8 <= 256, "barrier area");
 // After the stream the K ring and Q area hold the ordering scratch of the two
 // pairs: tmp 2048 x 8, bucket ids 2048 x 2, three 2048-word count arrays.
 constexpr int kPRankBytes = kTopK * 8 + kTopK * 2 + 3 * 2048 * 4;
@@ -91,7 +96,7 @@ struct PrefillParams {
   int32_t* handled;            // [B] out: 1 = row served here, 0 = left to the per-row kernel
 };
 
-// 18 warps: five of them share one SM sub-partition's 16384 registers, so
+// 19 warps: five of them share one SM sub-partition's 16384 registers, so
 // 96 registers per thread is the ceiling.
 template <int kMode>
 __global__ void __launch_bounds__(kPThreads, 1)
@@ -166,19 +171,19 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   const uint32_t bar_full = base_addr + kPOffBar;       // [kPStages]
   const uint32_t bar_empty = bar_full + 8 * kPStages;   // [kPStages]
-  const uint32_t bar_tfull = bar_empty + 8 * kPStages;  // [2]
-  const uint32_t bar_tempty = bar_tfull + 16;           // [2]
-  const uint32_t bar_q = bar_tempty + 16;               // [1]
+  const uint32_t bar_tfull = bar_empty + 8 * kPStages;  // [parity][pair]
+  const uint32_t bar_tempty = bar_tfull + 32;           // [parity][pair]
+  const uint32_t bar_q = bar_tempty + 32;               // [1]
 
   // ---- setup ----
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPStages; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, 1);  // the MMA commit: the epilogue never reads the K ring
+      ptx::mbar_init(bar_empty + 8 * s, 2);  // both issuers' MMA commits: the epilogue never reads the ring
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       ptx::mbar_init(bar_tfull + 8 * i, 1);
-      ptx::mbar_init(bar_tempty + 8 * i, 8);
+      ptx::mbar_init(bar_tempty + 8 * i, 4);  // the pair's four warps of the tile's parity
     }
     ptx::mbar_init(bar_q, 1);
     ptx::fence_mbar_init();
@@ -255,19 +260,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
       __syncwarp();
       issued = i + 1;
     }
-  } else if (warp == 1) {
-    // ===================== MMA issuer =====================
+  } else if (warp == 1 || warp == kPMmaWarp1) {
+    // ===================== MMA issuers, one per row pair =====================
+    // Each pair has its own TMEM buffers and barriers, so a pair that is
+    // cutting a candidate buffer holds up only its own MMAs; the other pair
+    // runs on until the ring (freed by both issuers' commits) is full.
+    const int q = warp == 1 ? 0 : 1;
     constexpr uint32_t idesc = ptx::idesc_e4m3_f32(kTileKeys, kPBufCols);
     bool ok = true;
     if (n_tiles > 0)
       ok = ptx::mbar_wait(bar_q, 0u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
-    const uint64_t qdesc = ptx::sw128_kmajor_desc(base_addr + kPOffQ);
+    const uint64_t qdesc = ptx::sw128_kmajor_desc(base_addr + kPOffQ + q * 2 * 8192);  // rows 128q..128q+127
 #pragma unroll 1
     for (int i = 0; i < n_tiles && !aborted; ++i) {
       const int s = i % kPStages;
       const uint32_t ph = static_cast<uint32_t>(i / kPStages) & 1u;
-      const int buf = i & 1;
+      const int buf = 2 * (i & 1) + q;
       const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
       ok = ptx::mbar_wait(bar_full + 8 * s, ph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns) &&
            ptx::mbar_wait(bar_tempty + 8 * buf, bph ^ 1u, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
@@ -388,18 +397,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
       float sc_A = 0.f, sc_B = 0.f;
       if (!aborted) {
         const uint32_t bph = static_cast<uint32_t>(i >> 1) & 1u;
-        const bool ok = ptx::mbar_wait(bar_tfull + 8 * par, bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
+        const bool ok = ptx::mbar_wait(bar_tfull + 8 * (2 * par + qp), bph, abort_flag, &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT,
                                        p.wait_ns);
         if (__any_sync(0xFFFFFFFFu, !ok)) aborted = true;
         if (!aborted) {
           __syncwarp();
           ptx::tc_fence_after();
-          const uint32_t ta = tmem + t_lane + static_cast<uint32_t>(par * kPBufCols);
-          if (live_A) sc_A = key_score(ta + static_cast<uint32_t>(jA * kHeads), w_A, scale);
-          if (live_B) sc_B = key_score(ta + static_cast<uint32_t>(jB * kHeads), w_B, scale);
+          const uint32_t ta = tmem + t_lane + static_cast<uint32_t>((2 * par + qp) * kPBufCols);
+          if (live_A) sc_A = key_score(ta, w_A, scale);
+          if (live_B) sc_B = key_score(ta + static_cast<uint32_t>(kHeads), w_B, scale);
           ptx::tc_fence_before();
           __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * par);
+          if (lane == 0) ptx::mbar_arrive(bar_tempty + 8 * (2 * par + qp));
         }
       }
       const uint32_t pos = tile_key0 + static_cast<uint32_t>(row);
@@ -465,10 +474,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
           ptx::mbar_wait(bar_full + 8 * (i % kPStages), static_cast<uint32_t>(i / kPStages) & 1u, &no_abort,
                          &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     }
-    if (warp == 1 && lane == 0 && mma_issued > 0) {
+    if ((warp == 1 || warp == kPMmaWarp1) && lane == 0 && mma_issued > 0) {
       const int last = mma_issued - 1;
-      ptx::mbar_wait(bar_tfull + 8 * (last & 1), static_cast<uint32_t>(last >> 1) & 1u, &no_abort, &g_dsa_status,
-                     DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
+      const int q = warp == 1 ? 0 : 1;
+      ptx::mbar_wait(bar_tfull + 8 * (2 * (last & 1) + q), static_cast<uint32_t>(last >> 1) & 1u, &no_abort,
+                     &g_dsa_status, DSA_STATUS_WAIT_TIMEOUT, p.wait_ns);
     }
     __syncthreads();
   }
@@ -476,7 +486,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kPTmemCols);
   }
-  if (warp < 2) return;
+  if (warp < 2 || warp >= kPMmaWarp1) return;
 
   // ---- tail: the eight warps of row pair `pair` select and order its two rows ----
   const int pair = ((warp - 2) >> 2) & 1;

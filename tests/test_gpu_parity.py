@@ -126,15 +126,26 @@ def _rows(w, idx):
     return w.rows(idx)
 
 
-def test_config3_full(pkg):
+# Configs 3 and 4 are causal rows of one sequence: by default they take the
+# shared-sequence kernel ("prefill+cluster"); DSA_TOPK_PREFILL=0 keeps them on
+# the per-row kernel alone.
+@pytest.mark.parametrize("prefill", ["default", "0"])
+def test_config3_full(pkg, prefill, monkeypatch):
+    if prefill == "0":
+        monkeypatch.setenv("DSA_TOPK_PREFILL", "0")
     assert_parity(pkg, workloads().config(3))
+    assert (pkg.last_path() == "prefill+cluster") == (prefill == "default")
 
 
-def test_config4_full(pkg):
+@pytest.mark.parametrize("prefill", ["default", "0"])
+def test_config4_full(pkg, prefill, monkeypatch):
     """All 2048 rows of config 4 (131072-key causal context, log-uniform
     scales) against the oracle."""
+    if prefill == "0":
+        monkeypatch.setenv("DSA_TOPK_PREFILL", "0")
     w = workloads().config(4)
     out, _ = assert_parity(pkg, w)
+    assert (pkg.last_path() == "prefill+cluster") == (prefill == "default")
     assert (out >= 0).all()  # every row has >= 2048 visible keys
     assert (np.diff(np.sort(out, axis=1), axis=1) > 0).all()  # unique per row
 

@@ -20,7 +20,9 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(autouse=True)
 def _prefill_on(monkeypatch):
-    """The stage is opt-in (DSA_TOPK_PREFILL=1); these tests turn it on."""
+    """By default the stage runs only when the block table must share pages
+    (more entries than four times the pool's pages); these tests turn it on
+    for every batch of 256+ rows (DSA_TOPK_PREFILL=1)."""
     monkeypatch.setenv("DSA_TOPK_PREFILL", "1")
 
 
