@@ -376,7 +376,9 @@ def main():
     # the inputs of step i+1 go up on one copy stream and the result of step
     # i-1 comes back on another while step i runs; K steps are timed as one
     # span, every step's copies inside it.
-    pipelined = not key_sharded and w.kcache_bytes() > 2 * torch.cuda.get_device_properties(dev).L2_cache_size
+    # Unique K bytes a step touches: its visible pages, at most the pool.
+    footprint = min(w.k_cache.numel() * w.k_cache.element_size(), w.kcache_bytes())
+    pipelined = not key_sharded and footprint > 2 * torch.cuda.get_device_properties(dev).L2_cache_size
     if not pipelined:
         def e2e_call():
             d_ins[0].copy_(h_in, non_blocking=True)
