@@ -276,6 +276,17 @@ def test_forced_cluster_sizes_l2_resident(pkg, g, monkeypatch):
     assert_parity(pkg, _rows(w, list(range(0, 192, 3))))
 
 
+@pytest.mark.parametrize("g", [2, 4, 8, 16])
+def test_cluster_select_small_rows(pkg, g, monkeypatch):
+    """Rows of up to a few thousand keys spread over 2 to 16 CTAs: every key
+    is a candidate (no CTA fills its buffer), so the cluster select runs on
+    totals around and below 2048 and 4096, including rows with fewer keys
+    than CTAs and an empty row."""
+    monkeypatch.setenv("DSA_TOPK_CLUSTER", str(g))
+    w = workloads().custom([1, 700, 2047, 2048, 2049, 3000, 4095, 4096, 4097, 4200, 6000, 0], seed=91)
+    assert_parity(pkg, w)
+
+
 @pytest.mark.parametrize("split", ["0", "1"])
 def test_cluster_two_class_launch(pkg, split, monkeypatch):
     """Cluster path on a batch that needs more clusters than fit at once:
