@@ -50,8 +50,10 @@ def traffic_per_launch(config, kernel):
 
 
 DOMINANT = {"cluster": "dsa::indexer_kernel<0>", "cluster-split": "dsa::indexer_kernel<0>",
+            "cluster-tail": "dsa::indexer_kernel<0>",
             "prefill+cluster": "dsa::prefill_kernel<0> + dsa::indexer_kernel<0>"}
 DOMINANT_PARTIAL = {"cluster": "dsa::indexer_kernel<2>", "cluster-split": "dsa::indexer_kernel<2>",
+                    "cluster-tail": "dsa::indexer_kernel<2>",
                     "prefill+cluster": "dsa::prefill_kernel<2> + dsa::indexer_kernel<2>"}
 PREFILL_CONFIGS = (3, 4)
 # Configs whose single sequence is split along the key axis across ranks

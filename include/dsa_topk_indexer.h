@@ -201,7 +201,9 @@ DSA_API int dsa_topk_indexer_last_launch_count(void);
 
 /* Schedule the last successful top-K call on this host thread took:
  * "cluster" (one cluster kernel, optionally after the longest-first plan),
- * "cluster-split" (two concurrent cluster kernels), "prefill+cluster" (the
+ * "cluster-split" (two concurrent cluster kernels, the longest rows with more
+ * CTAs), "cluster-tail" (two cluster kernels, the rows of the last partial
+ * wave with more CTAs), "prefill+cluster" (the
  * shared-sequence kernel, then the cluster kernel for the rows it left) or
  * "noalloc" (the no-allocation entry point's cluster kernel). */
 DSA_API const char* dsa_topk_indexer_last_path(void);

@@ -439,6 +439,39 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
         launches = 2;
       }
     }
+    // Several waves of G-CTA clusters end in a partial wave that holds the
+    // shortest rows and fills the GPU poorly. Those rows run as a second
+    // launch with more CTAs per row, issued after the first on a second
+    // stream, so that their clusters take the slots of the first launch's
+    // last wave as they free (DSA_TOPK_TAIL=0 turns this off). Measured on
+    // B200 for config 2 (512 rows: three waves of 148 two-CTA clusters, then
+    // 68 rows that filled 136 of 296 slots; now at 4 CTAs each): 0.800 ->
+    // 0.776 ms.
+    if (order && G <= 2) {
+      const int64_t per_wave = (2 * static_cast<int64_t>(num_sms)) / G;
+      const int64_t rem = prm.batch % per_wave;
+      int64_t g_tail = rem > 0 ? (2 * static_cast<int64_t>(num_sms)) / rem : 0;
+      if (g_tail > 8) g_tail = 8;
+      const char* tail_env = std::getenv("DSA_TOPK_TAIL");
+      cudaStream_t side = nullptr;
+      cudaEvent_t fork = nullptr, join = nullptr;
+      if (prm.batch > per_wave && g_tail > G && !(tail_env && tail_env[0] == '0') &&
+          side_stream(stream, &side, &fork, &join)) {
+        KernelTimer timer(stream);
+        if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
+          return DSA_ERR_CUDA;
+        IndexerParams tail = params;
+        tail.order = order + (prm.batch - rem);
+        if ((rc = launch(params, prm.batch - rem, G, stream)) != DSA_OK) return rc;
+        if ((rc = launch(tail, rem, static_cast<int>(g_tail), side)) != DSA_OK) return rc;
+        if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)
+          return DSA_ERR_CUDA;
+        timer.stop();
+        t_last_launches = launches + 1;
+        t_last_path = "cluster-tail";
+        return DSA_OK;
+      }
+    }
     if (order || params.order_base >= 0) {
       // When the short rows fit at two CTAs each, run everything in one
       // wave: the R longest rows at G CTAs and the rest at 2, as two

@@ -287,6 +287,19 @@ def test_cluster_select_small_rows(pkg, g, monkeypatch):
     assert_parity(pkg, w)
 
 
+@pytest.mark.parametrize("tail", ["0", "1"])
+def test_cluster_tail_launch(pkg, tail, monkeypatch):
+    """A batch of 300 rows at two CTAs per row: two waves of 148 clusters and
+    a partial one of 4 rows, which run as a second launch at 8 CTAs per row
+    (tail=1) or in the last wave of the single launch (tail=0)."""
+    monkeypatch.setenv("DSA_TOPK_TAIL", tail)
+    g = torch.Generator().manual_seed(93)
+    sl = torch.randint(1, 9000, (300,), generator=g).to(torch.int32)
+    w = workloads().custom(sl.tolist(), seed=94)
+    assert_parity(pkg, w)
+    assert (pkg.last_path() == "cluster-tail") == (tail == "1")
+
+
 @pytest.mark.parametrize("split", ["0", "1"])
 def test_cluster_two_class_launch(pkg, split, monkeypatch):
     """Cluster path on a batch that needs more clusters than fit at once:
