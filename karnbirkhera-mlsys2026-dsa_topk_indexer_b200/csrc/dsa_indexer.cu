@@ -353,6 +353,8 @@ int check_common(const void* q, const void* kcache, const float* w, const int32_
 // row) never take it: its launches would add ~10 us for nothing.
 // DSA_TOPK_PREFILL=0 turns it off, =1 tries it on any batch of 256+ rows.
 constexpr int64_t kPrefillMinRows = 256;
+// Cluster sizes up to which the last partial wave runs as its own launch.
+constexpr int kTailMaxG = 4;
 constexpr int64_t kPrefillShareFactor = 4;
 
 template <int kMode>
@@ -446,8 +448,9 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
     // last wave as they free (DSA_TOPK_TAIL=0 turns this off). Measured on
     // B200 for config 2 (512 rows: three waves of 148 two-CTA clusters, then
     // 68 rows that filled 136 of 296 slots; now at 4 CTAs each): 0.800 ->
-    // 0.776 ms.
-    if (order && G <= 2) {
+    // 0.776 ms; 128-row batches at 4 CTAs (54 rows at 5): 0.260 -> 0.253 ms.
+    // It takes precedence over the two-class launch below.
+    if ((order || params.order_base >= 0) && G <= kTailMaxG) {
       const int64_t per_wave = (2 * static_cast<int64_t>(num_sms)) / G;
       const int64_t rem = prm.batch % per_wave;
       int64_t g_tail = rem > 0 ? (2 * static_cast<int64_t>(num_sms)) / rem : 0;
@@ -461,7 +464,10 @@ int launch_indexer(const void* q, const void* kcache, const IndexerParams& prm, 
         if (cudaEventRecord(fork, stream) != cudaSuccess || cudaStreamWaitEvent(side, fork, 0) != cudaSuccess)
           return DSA_ERR_CUDA;
         IndexerParams tail = params;
-        tail.order = order + (prm.batch - rem);
+        if (order)
+          tail.order = order + (prm.batch - rem);
+        else
+          tail.order_base = static_cast<int32_t>(prm.batch - rem);
         if ((rc = launch(params, prm.batch - rem, G, stream)) != DSA_OK) return rc;
         if ((rc = launch(tail, rem, static_cast<int>(g_tail), side)) != DSA_OK) return rc;
         if (cudaEventRecord(join, side) != cudaSuccess || cudaStreamWaitEvent(stream, join, 0) != cudaSuccess)

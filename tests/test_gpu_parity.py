@@ -300,6 +300,17 @@ def test_cluster_tail_launch(pkg, tail, monkeypatch):
     assert (pkg.last_path() == "cluster-tail") == (tail == "1")
 
 
+def test_cluster_tail_launch_ranked_in_kernel(pkg):
+    """128 rows at four CTAs per row (rows ranked inside the kernel, no plan
+    launch): a wave of 74 clusters, then 54 rows as a second launch at five
+    CTAs per row."""
+    g = torch.Generator().manual_seed(95)
+    sl = torch.randint(1, 20000, (128,), generator=g).to(torch.int32)
+    w = workloads().custom(sl.tolist(), seed=96)
+    assert_parity(pkg, w)
+    assert pkg.last_path() == "cluster-tail"
+
+
 @pytest.mark.parametrize("split", ["0", "1"])
 def test_cluster_two_class_launch(pkg, split, monkeypatch):
     """Cluster path on a batch that needs more clusters than fit at once:
