@@ -240,8 +240,8 @@ def last_launch_count():
 
 
 def last_path():
-    """Schedule of the last top-K call on this thread: "segmented", "cluster"
-    or "cluster-split"."""
+    """Schedule of the last top-K call on this thread: "cluster",
+    "cluster-split", "cluster-tail", "prefill+cluster" or "noalloc"."""
     return _lib.load().dsa_topk_indexer_last_path().decode()
 
 

@@ -317,7 +317,6 @@ def test_cluster_two_class_launch(pkg, split, monkeypatch):
     the longest rows at the default cluster size and the rest at two CTAs
     each, launched concurrently on two streams (split=1), or all rows at one
     size in longest-first order (split=0)."""
-    monkeypatch.setenv("DSA_TOPK_PATH", "cluster")
     monkeypatch.setenv("DSA_TOPK_SPLIT", split)
     w = workloads().custom([32768, 600, 0, 17000, 2049, 9000, 100, 24000] * 8, seed=31)
     assert_parity(pkg, w)
@@ -339,10 +338,13 @@ def test_two_class_launch_decided_on_device(pkg, kind):
 
 @pytest.mark.parametrize("cfg", [1, 3])
 def test_cluster_kernel_path(pkg, cfg, monkeypatch):
-    """The one-launch cluster kernel (used when no workspace can be had, and
-    by the no-allocation entry point) stays parity-green."""
-    monkeypatch.setenv("DSA_TOPK_PATH", "cluster")
+    """The one-launch cluster kernel (the schedule when the two-class and
+    last-wave launches are off, and that of the no-allocation entry point)
+    stays parity-green."""
+    monkeypatch.setenv("DSA_TOPK_SPLIT", "0")
+    monkeypatch.setenv("DSA_TOPK_TAIL", "0")
     w = workloads().config(cfg)
     if cfg == 3:
         w = _rows(w, list(range(0, 8192, 37)))
     assert_parity(pkg, w)
+    assert pkg.last_path() == "cluster"
