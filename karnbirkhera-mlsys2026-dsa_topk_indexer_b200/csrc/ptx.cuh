@@ -77,21 +77,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
-// Shared-memory load that the compiler keeps in program order with the other
-// volatile asm statements (e.g. an mbarrier arrive that releases the buffer
-// it reads from); a plain C++ load may be sunk to its first use.
-__device__ __forceinline__ float lds_f32_ordered(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
-// Orders this thread's generic-proxy shared-memory accesses before later
-// async-proxy (TMA, tcgen05) accesses to the same memory.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // --------------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
