@@ -5,15 +5,17 @@
 // dimension) and the tiles are split evenly over the G CTAs. Each CTA is
 // warp-specialised (10 warps):
 //   warp 0      TMA producer: per tile, two 8 KB page-data boxes (128-byte
-//               swizzle) and two 256 B scale rows into a 4-stage ring;
+//               swizzle) into a 4-stage ring, a stage freed by the MMA commit;
 //   warp 1      TMEM owner and MMA issuer: D[128 keys x 64 heads] (fp32 in
 //               TMEM, 4 buffers) = K_tile[128 x 128 e4m3] . Q[64 x 128 e4m3]^T
 //               as four tcgen05.mma kind::f8f6f4 (K = 32 each);
 //   warps 2..9  two epilogue groups of four warps (even / odd tiles): thread =
 //               TMEM lane = key; tcgen05.ld of its 64 head columns, relu /
 //               head-weight / scale reduction in registers (packed fp32x2
-//               FMA), then a threshold filter into a shared-memory candidate
-//               buffer that is cut back towards the best 2048 when it fills;
+//               FMA; the key's scale from its own global load, issued two
+//               tiles ahead), then a threshold filter into a shared-memory
+//               candidate buffer that is cut back to the best 2048 when it
+//               fills;
 //   all warps   after the stream: cluster-wide exact radix select of the best
 //               2048 over every CTA's candidates (histograms summed through
 //               distributed shared memory), survivors written into CTA 0's
