@@ -116,3 +116,23 @@ def test_prefill_partial_merge_equals_direct(pkg):
     torch.cuda.synchronize()
     assert pkg.device_status(0, clear=True) == 0
     assert np.array_equal(merged.cpu().numpy(), direct.cpu().numpy())
+
+
+def test_prefill_nan_input_bytes(pkg):
+    """e4m3 NaN bytes on the shared-sequence path: one key seen by every row,
+    and one NaN head in the queries of a whole group (rows in both the first
+    and second slot of each row pair, whose scores take different code: the
+    second row hands its TMEM columns back before its last heads are
+    reduced). relu maps every NaN product to 0, as on the per-row kernel."""
+    w = workloads().make_shared("nan", 256, 6000, 100, 9)
+    page = int(w.block_table[0, 3])
+    w.k_cache[page, 10, 0, 5] = 0x7F            # key 3*64+10, visible to every row
+    q8 = w.q.view(torch.uint8)
+    # group 2 (rows 8..11: first / second slot of both pairs); heads 3, 22
+    # and 54 are heads whose relu takes the x + |x| form, in the first (3,
+    # 22) and the second half (54) of the 64
+    for r, h in ((8, 3), (9, 22), (10, 37), (11, 54)):
+        q8[r, h, 40] = 0x7F
+    q8[201, 62, 0] = 0xFF                        # a second-slot row of another group
+    _, path = _check(pkg, w)
+    assert path == "prefill+cluster"
