@@ -58,6 +58,7 @@ extern "C" {
 #define DSA_STATUS_WAIT_TIMEOUT 0x1u /* a pipeline wait gave up (kernel ended early) */
 #define DSA_STATUS_BAD_PAGE 0x2u     /* block_table held an id outside [0, num_pages) */
 #define DSA_STATUS_SEQ_CLAMPED 0x4u  /* seq_len > max_pages*64; clamped              */
+#define DSA_STATUS_BAD_RECORD 0x8u   /* a decode-queue record held an invalid event or row; skipped */
 
 /*
  * The indexer: scores every visible key of every request and writes the
@@ -169,6 +170,41 @@ DSA_API int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe, co
                                         const void* kpe_cache, const int32_t* sparse_indices, float sm_scale,
                                         void* output, float* lse, int64_t num_tokens, int64_t num_indices,
                                         int64_t num_pages, void* stream);
+
+/* Device work queue across decode steps. The request table stays in device
+ * memory between steps: req_len [num_slots] int32 (-1 = slot not in use)
+ * and req_block_table [num_slots, max_pages] int32 page ids. A step ships
+ * one record (int32 words, device memory, `record_words` capacity):
+ *   [0] words used   [1] events   [2] batch B   [3] advance (>= 0)
+ *   [4] offset of the batch list  [5..7] 0
+ *   events from word DSA_QUEUE_HEADER_WORDS, 4 words each, in order:
+ *     {DSA_QUEUE_ADMIT, slot, length, n}  followed by n page ids, padded
+ *                                          with zeros to a multiple of 4 words
+ *     {DSA_QUEUE_APPEND_PAGE, slot, page_index, page_id}
+ *     {DSA_QUEUE_SET_LEN, slot, length, 0}
+ *     {DSA_QUEUE_RETIRE, slot, 0, 0}
+ *   the batch list: B distinct slots, at the offset in word [4].
+ * The call applies the events, then for every batch row b adds `advance` to
+ * req_len[slot_b] and writes seq_lens[b] (the new length) and the row's
+ * visible entries block_table[b, 0 .. ceil(len/64)) (width max_pages);
+ * rows B .. capacity-1 get seq_lens 0, so the indexer over `capacity` rows
+ * returns -1 for them. Events or rows naming a slot outside [0, num_slots),
+ * a slot not in use, or a page index outside [0, max_pages) are skipped and
+ * raise DSA_STATUS_BAD_RECORD; a record whose header or event list cannot
+ * be read is dropped whole. A slot listed twice in one batch is advanced an
+ * unspecified number of times. Two launches (one CTA, then `capacity` CTAs),
+ * asynchronous on `stream`, no allocation, capturable into a CUDA graph
+ * together with the indexer call that consumes seq_lens / block_table. No
+ * counterpart in the reference, whose entry point takes a host-built batch
+ * per call (solution/cuda/kernel.cu:818-887). */
+#define DSA_QUEUE_HEADER_WORDS 8
+#define DSA_QUEUE_ADMIT 1
+#define DSA_QUEUE_APPEND_PAGE 2
+#define DSA_QUEUE_SET_LEN 3
+#define DSA_QUEUE_RETIRE 4
+DSA_API int dsa_decode_queue_apply(const int32_t* record, int64_t record_words, int32_t* req_len,
+                                   int32_t* req_block_table, int64_t num_slots, int64_t max_pages,
+                                   int32_t* seq_lens, int32_t* block_table, int64_t capacity, void* stream);
 
 /* Test hook for the bounded-wait abort path (off by default). Every
  * pipeline wait of the indexer kernels gives up after a time limit (2 s),

@@ -13,7 +13,7 @@ The package directory name is not a Python identifier; import it with
 import ctypes
 
 from . import _lib
-from ._lib import (DSA_STATUS_BAD_PAGE, DSA_STATUS_SEQ_CLAMPED,  # noqa: F401
+from ._lib import (DSA_STATUS_BAD_PAGE, DSA_STATUS_BAD_RECORD, DSA_STATUS_SEQ_CLAMPED,  # noqa: F401
                    DSA_STATUS_WAIT_TIMEOUT)
 
 HEADS = 64
@@ -22,7 +22,8 @@ PAGE_SIZE = 64
 PAGE_BYTES = 8448
 TOPK = 2048
 
-__all__ = ["launch_topk_c", "indexer_scores", "indexer_partial", "indexer_merge", "sparse_attention", "device_status",
+__all__ = ["launch_topk_c", "indexer_scores", "indexer_partial", "indexer_merge", "sparse_attention",
+           "decode_queue_apply", "device_status",
            "last_launch_count", "HEADS", "HEAD_DIM", "PAGE_SIZE", "PAGE_BYTES", "TOPK"]
 
 
@@ -225,6 +226,35 @@ def sparse_attention(q_nope, q_pe, ckv_cache, kpe_cache, sparse_indices, sm_scal
                                              _stream(dev))
     _lib.check(rc, "sparse_attention")
     return output, lse
+
+
+def decode_queue_apply(record, req_len, req_block_table, seq_lens, block_table):
+    """Applies one decode-queue record on the device (C ABI
+    dsa_decode_queue_apply): the record's events update the request table
+    (req_len [S] int32, -1 = free; req_block_table [S, max_pages] int32),
+    then every batch row's request advances and its length and visible
+    block-table entries are written to seq_lens [C] / block_table
+    [C, max_pages] (rows past the batch: length 0). All int32, contiguous,
+    on one CUDA device; record [W] int32 in the layout the C header gives
+    (decode_queue.QueueRecord builds it)."""
+    torch = _torch()
+    dev = record.device
+    _require(dev.type == "cuda", "record must be a CUDA tensor")
+    for name, t in (("record", record), ("req_len", req_len), ("req_block_table", req_block_table),
+                    ("seq_lens", seq_lens), ("block_table", block_table)):
+        _require(t.dtype == torch.int32 and t.is_contiguous() and t.device == dev,
+                 f"{name} must be contiguous int32 on {dev}")
+    _require(req_block_table.dim() == 2 and req_block_table.shape[0] == req_len.numel(),
+             "req_block_table must be [num_slots, max_pages]")
+    _require(block_table.dim() == 2 and block_table.shape[1] == req_block_table.shape[1]
+             and block_table.shape[0] == seq_lens.numel(), "block_table must be [capacity, max_pages]")
+    lib = _lib.load()
+    _select(lib, dev)
+    with torch.cuda.device(dev):
+        rc = lib.dsa_decode_queue_apply(_ptr(record), record.numel(), _ptr(req_len), _ptr(req_block_table),
+                                        req_len.numel(), req_block_table.shape[1], _ptr(seq_lens), _ptr(block_table),
+                                        seq_lens.numel(), _stream(dev))
+    _lib.check(rc, "decode_queue_apply")
 
 
 def device_status(device=0, clear=True):

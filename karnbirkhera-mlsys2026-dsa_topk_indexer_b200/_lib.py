@@ -16,6 +16,14 @@ DSA_NOALLOC_MAX_BATCH = 65536
 DSA_STATUS_WAIT_TIMEOUT = 0x1
 DSA_STATUS_BAD_PAGE = 0x2
 DSA_STATUS_SEQ_CLAMPED = 0x4
+DSA_STATUS_BAD_RECORD = 0x8
+
+# Decode-queue record format (dsa_decode_queue_apply).
+DSA_QUEUE_HEADER_WORDS = 8
+DSA_QUEUE_ADMIT = 1
+DSA_QUEUE_APPEND_PAGE = 2
+DSA_QUEUE_SET_LEN = 3
+DSA_QUEUE_RETIRE = 4
 
 # (name, restype, argtypes) for every function the header declares.
 _P, _I64, _I32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -32,6 +40,7 @@ SIGNATURES = [
     ("dsa_topk_indexer_last_launch_count", _I32, []),
     ("dsa_topk_indexer_last_path", ctypes.c_char_p, []),
     ("dsa_index_cache_write", _I32, [_P, _I32, _P, _P, _I64, _I64, _P]),
+    ("dsa_decode_queue_apply", _I32, [_P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P]),
     ("dsa_sparse_attention_launch", _I32, [_P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_set_timing", _I32, [_I32]),
     ("dsa_topk_indexer_kernel_ms", _I32, [ctypes.POINTER(ctypes.c_float)]),

@@ -19,6 +19,7 @@
 #include "prefill_kernel.cuh"
 #include "cache_writer.cuh"
 #include "sparse_attention.cuh"
+#include "decode_queue.cuh"
 
 namespace dsa {
 
@@ -810,6 +811,29 @@ extern "C" int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* 
         k, slots, static_cast<uint8_t*>(k_cache), num_tokens, num_pages);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   t_last_launches = 1;
+  return DSA_OK;
+}
+
+extern "C" int dsa_decode_queue_apply(const int32_t* record, int64_t record_words, int32_t* req_len,
+                                      int32_t* req_block_table, int64_t num_slots, int64_t max_pages,
+                                      int32_t* seq_lens, int32_t* block_table, int64_t capacity, void* stream) {
+  t_last_launches = 0;
+  t_timed = false;
+  if (!record || !req_len || !req_block_table || !seq_lens || !block_table) return DSA_ERR_INVALID_ARG;
+  if (record_words < DSA_QUEUE_HEADER_WORDS || num_slots < 1 || num_slots > INT32_MAX || max_pages < 1 ||
+      max_pages > INT32_MAX / 64 || capacity < 1 || capacity > INT32_MAX)
+    return DSA_ERR_INVALID_ARG;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int32_t mp = static_cast<int32_t>(max_pages);
+  decode_queue_apply_kernel<<<1, kQueueThreads, 0, st>>>(record, record_words, req_len, req_block_table, num_slots,
+                                                        mp, capacity);
+  decode_queue_gather_kernel<<<static_cast<unsigned>(capacity), kQueueThreads, 0, st>>>(
+      record, record_words, req_len, req_block_table, num_slots, mp, seq_lens, block_table, capacity);
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = 2;
   return DSA_OK;
 }
 

@@ -1,0 +1,259 @@
+"""Device work queue across decode steps.
+
+A serving loop runs the indexer once per decode step over the requests in
+flight. Between steps a request's length grows by one token, its block table
+gains a page every 64 tokens, and requests are admitted and retired. Shipping
+every step's full block table ([B, max_pages] int32: 4 MB for B = 512 at 2048
+pages) is wasted work when almost nothing changed, so here:
+
+- the request table (length and block-table row of each request slot) lives
+  in device memory for the whole run;
+- a step sends one small record: the events since the last step (admit a
+  request with its page list, append one page, set a length, retire) and the
+  step's batch as a list of slots (int32 words; layout in
+  include/dsa_topk_indexer.h, dsa_decode_queue_apply);
+- one CUDA graph per batch-size bucket replays [apply the record and gather
+  the batch rows (two small kernels), the indexer over the gathered batch]
+  with fixed device buffers, so a step is one small host-to-device copy and
+  one replay, with no synchronisation between steps.
+
+`RequestTable` is the host's mirror (validation, page bookkeeping, the
+record encoder) and needs no GPU; `DecodeQueue` is the device runner.
+
+    dq = DecodeQueue(k_cache, num_slots=512, max_pages=2048, max_batch=512)
+    dq.admit(slot=3, seq_len=5000, pages=[...79 page ids...])
+    dq.append_page(3, page_id)               # when the request reaches its next page
+    topk = dq.step(slots, q, weights)        # lengths += 1, then the indexer
+    dq.retire(3)
+
+The reference has no counterpart: its entry point takes a host-built batch
+on every call (solution/cuda/kernel.cu:818-887).
+"""
+import importlib
+
+from ._lib import (DSA_QUEUE_ADMIT, DSA_QUEUE_APPEND_PAGE, DSA_QUEUE_HEADER_WORDS, DSA_QUEUE_RETIRE,
+                   DSA_QUEUE_SET_LEN)
+from .graph_runner import bucket_for, bucket_sizes
+
+PAGE, TOPK, HEADS, DIM = 64, 2048, 64, 128
+
+
+class RequestTable:
+    """Host mirror of the device request table and encoder of step records.
+
+    Every change is validated here, before it is queued: slots in
+    [0, num_slots), admissions only into free slots, pages appended in order
+    and at most max_pages per request, and a step only over distinct
+    requests in use whose advanced length stays within their pages."""
+
+    def __init__(self, num_slots, max_pages):
+        if num_slots < 1 or max_pages < 1:
+            raise ValueError("num_slots and max_pages must be positive")
+        self.num_slots, self.max_pages = int(num_slots), int(max_pages)
+        self.lens = [-1] * self.num_slots      # -1: slot free
+        self.pages = [[] for _ in range(self.num_slots)]
+        self.events = []                       # int32 words queued for the next record
+
+    def _slot(self, slot):
+        slot = int(slot)
+        if not 0 <= slot < self.num_slots:
+            raise ValueError(f"slot {slot} outside [0, {self.num_slots})")
+        return slot
+
+    def _in_use(self, slot):
+        slot = self._slot(slot)
+        if self.lens[slot] < 0:
+            raise ValueError(f"slot {slot} holds no request")
+        return slot
+
+    def admit(self, slot, seq_len, pages):
+        slot = self._slot(slot)
+        if self.lens[slot] >= 0:
+            raise ValueError(f"slot {slot} is in use; retire it first")
+        pages = [int(p) for p in pages]
+        if len(pages) > self.max_pages:
+            raise ValueError(f"{len(pages)} pages exceed max_pages {self.max_pages}")
+        if not 0 <= int(seq_len) <= PAGE * len(pages):
+            raise ValueError(f"seq_len {seq_len} does not fit {len(pages)} pages")
+        pad = (-len(pages)) % 4
+        self.events += [DSA_QUEUE_ADMIT, slot, int(seq_len), len(pages)] + pages + [0] * pad
+        self.lens[slot], self.pages[slot] = int(seq_len), pages
+
+    def append_page(self, slot, page_id):
+        slot = self._in_use(slot)
+        idx = len(self.pages[slot])
+        if idx >= self.max_pages:
+            raise ValueError(f"slot {slot} already holds max_pages {self.max_pages} pages")
+        self.events += [DSA_QUEUE_APPEND_PAGE, slot, idx, int(page_id)]
+        self.pages[slot].append(int(page_id))
+
+    def set_len(self, slot, seq_len):
+        slot = self._in_use(slot)
+        if not 0 <= int(seq_len) <= PAGE * len(self.pages[slot]):
+            raise ValueError(f"seq_len {seq_len} does not fit the {len(self.pages[slot])} pages of slot {slot}")
+        self.events += [DSA_QUEUE_SET_LEN, slot, int(seq_len), 0]
+        self.lens[slot] = int(seq_len)
+
+    def retire(self, slot):
+        slot = self._in_use(slot)
+        self.events += [DSA_QUEUE_RETIRE, slot, 0, 0]
+        self.lens[slot], self.pages[slot] = -1, []
+
+    def check_step(self, slots, advance):
+        """Raises if the step cannot run; leaves the mirror unchanged."""
+        slots = [self._in_use(s) for s in slots]
+        if len(set(slots)) != len(slots):
+            raise ValueError("a slot is listed twice in one step")
+        if advance < 0:
+            raise ValueError("advance must be >= 0")
+        for s in slots:
+            if self.lens[s] + advance > PAGE * len(self.pages[s]):
+                raise ValueError(f"slot {s}: length {self.lens[s] + advance} needs a page it has not been given")
+        return slots
+
+    def build_record(self, slots, advance=1):
+        """The step's record (list of int32 words); applies the advance to
+        the mirror and clears the queued events."""
+        slots = self.check_step(slots, advance)
+        ev = self.events
+        n_events = 0
+        i = 0
+        while i < len(ev):  # count events (an admission carries its padded page list)
+            n_events += 1
+            i += 4 + ((ev[i + 3] + 3) // 4 * 4 if ev[i] == DSA_QUEUE_ADMIT else 0)
+        batch_off = DSA_QUEUE_HEADER_WORDS + len(ev)
+        words = batch_off + len(slots)
+        rec = [words, n_events, len(slots), int(advance), batch_off, 0, 0, 0] + ev + slots
+        for s in slots:
+            self.lens[s] += int(advance)
+        self.events = []
+        return rec
+
+    def batch_inputs(self, slots):
+        """(seq_lens [B], block_table [B, max_pages]) of the listed requests
+        as the mirror holds them (zeros past each row's pages), as numpy."""
+        import numpy as np
+        sl = np.array([self.lens[s] for s in slots], dtype=np.int32)
+        bt = np.zeros((len(slots), self.max_pages), dtype=np.int32)
+        for b, s in enumerate(slots):
+            bt[b, :len(self.pages[s])] = self.pages[s]
+        return sl, bt
+
+
+class DecodeQueue:
+    """Device runner over a RequestTable (see the module docstring).
+
+    k_cache [num_pages, 64, 1, 132] is the serving system's paged index-K
+    cache, fixed for the runner's life (it is captured into the graphs).
+    Records are staged through a ring of `ring` pinned host buffers of
+    `record_words` int32 words; a step whose record is larger raises
+    (admit fewer requests per step). `step` returns a view of the bucket's
+    output rows, valid until the next step that uses the same bucket."""
+
+    def __init__(self, k_cache, num_slots, max_pages, max_batch, record_words=1 << 18, buckets=None, ring=4,
+                 stream=None):
+        import torch
+        self.torch = torch
+        self.pkg = importlib.import_module(__package__)
+        self.k_cache = k_cache
+        self.dev = k_cache.device
+        self.table = RequestTable(num_slots, max_pages)
+        self.max_pages = int(max_pages)
+        self.sizes = list(buckets) if buckets else bucket_sizes(max_batch)
+        self.stream = stream or torch.cuda.Stream(self.dev)
+        self.record_words = int(record_words)
+        if self.record_words < DSA_QUEUE_HEADER_WORDS + max(self.sizes):
+            raise ValueError("record_words cannot hold the largest batch list")
+        i32 = torch.int32
+        self.req_len = torch.full((num_slots,), -1, dtype=i32, device=self.dev)
+        self.req_bt = torch.zeros((num_slots, self.max_pages), dtype=i32, device=self.dev)
+        self.record = torch.zeros(self.record_words, dtype=i32, device=self.dev)
+        self.idle_record = torch.zeros(DSA_QUEUE_HEADER_WORDS, dtype=i32, device=self.dev)  # no events, no rows
+        self.idle_record[0] = DSA_QUEUE_HEADER_WORDS
+        self.idle_record[4] = DSA_QUEUE_HEADER_WORDS
+        self.pinned = [torch.zeros(self.record_words, dtype=i32).pin_memory() for _ in range(int(ring))]
+        self.copied = [None] * int(ring)
+        self.next_ring = 0
+        self.graphs = {}
+
+    # request bookkeeping (queued, sent with the next step's record)
+    def admit(self, slot, seq_len, pages):
+        self.table.admit(slot, seq_len, pages)
+
+    def append_page(self, slot, page_id):
+        self.table.append_page(slot, page_id)
+
+    def set_len(self, slot, seq_len):
+        self.table.set_len(slot, seq_len)
+
+    def retire(self, slot):
+        self.table.retire(slot)
+
+    def _buffers(self, size):
+        torch = self.torch
+        return {
+            "q": torch.zeros((size, HEADS, DIM), dtype=torch.float8_e4m3fn, device=self.dev),
+            "w": torch.zeros((size, HEADS), dtype=torch.float32, device=self.dev),
+            "sl": torch.zeros((size,), dtype=torch.int32, device=self.dev),
+            "bt": torch.zeros((size, self.max_pages), dtype=torch.int32, device=self.dev),
+            "out": torch.empty((size, TOPK), dtype=torch.int32, device=self.dev),
+        }
+
+    def _run(self, bufs, record):
+        self.pkg.decode_queue_apply(record, self.req_len, self.req_bt, bufs["sl"], bufs["bt"])
+        self.pkg.launch_topk_c(bufs["q"], self.k_cache, bufs["w"], bufs["sl"], bufs["bt"], bufs["out"])
+
+    def _capture(self, size):
+        torch = self.torch
+        bufs = self._buffers(size)
+        self.stream.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(self.stream):
+            self._run(bufs, self.idle_record)  # warm-up outside capture (library workspaces); changes nothing
+        self.stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self._run(bufs, self.record)
+        self.graphs[size] = (g, bufs)
+        return self.graphs[size]
+
+    def step(self, slots, q, weights, advance=1):
+        """One decode step over the requests in `slots` (batch order): their
+        lengths grow by `advance`, then the indexer runs with q [B, 64, 128]
+        e4m3 and weights [B, 64] fp32 (device or pinned host tensors).
+        Returns the [B, 2048] top-K slots (a view, see the class docstring)."""
+        torch = self.torch
+        slots = [int(s) for s in slots]
+        B = len(slots)
+        if B == 0:
+            raise ValueError("empty step")
+        if tuple(q.shape) != (B, HEADS, DIM) or tuple(weights.shape) != (B, HEADS):
+            raise ValueError("q must be [B, 64, 128] and weights [B, 64] for the B listed slots")
+        size = bucket_for(B, self.sizes)
+        self.table.check_step(slots, advance)
+        n = DSA_QUEUE_HEADER_WORDS + len(self.table.events) + B
+        if n > self.record_words:
+            raise ValueError(f"step record of {n} words exceeds record_words {self.record_words}")
+        g, bufs = self.graphs.get(size) or self._capture(size)
+        rec = self.table.build_record(slots, advance)
+        j = self.next_ring
+        self.next_ring = (j + 1) % len(self.pinned)
+        if self.copied[j] is not None:
+            self.copied[j].synchronize()  # the copy that last read this pinned buffer has finished
+        self.pinned[j][:n] = torch.tensor(rec, dtype=torch.int32)
+        cur = torch.cuda.current_stream(self.dev)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self.record[:n].copy_(self.pinned[j][:n], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+            self.copied[j] = ev
+            bufs["q"][:B].copy_(q, non_blocking=True)
+            bufs["w"][:B].copy_(weights, non_blocking=True)
+            g.replay()
+        cur.wait_stream(self.stream)
+        return bufs["out"][:B]
+
+    def device_table(self):
+        """(req_len, req_block_table) as the device holds them (synchronises)."""
+        self.torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        return self.req_len.cpu(), self.req_bt.cpu()

@@ -82,3 +82,22 @@ def test_missing_library_fails_loudly(monkeypatch):
         pkg._lib.load()
     with pytest.raises(RuntimeError):
         pkg.last_launch_count()
+
+
+def test_queue_constants_match_header():
+    """The decode-queue record constants of the Python binding equal the
+    header's #defines (the record is built on the host, read on the GPU)."""
+    text = open(os.path.join(ROOT, "include", "dsa_topk_indexer.h")).read()
+    defs = dict(re.findall(r"#define\s+(DSA_(?:QUEUE|STATUS)_\w+)\s+(0x[0-9a-f]+|\d+)u?", text))
+    lib = package()._lib
+    for name, val in defs.items():
+        assert getattr(lib, name) == int(val, 0), name
+
+
+def test_queue_apply_argument_errors(lib):
+    P = ctypes.c_void_p
+    ok = P(16)
+    assert lib.dsa_decode_queue_apply(None, 64, ok, ok, 4, 8, ok, ok, 4, None) == 1
+    assert lib.dsa_decode_queue_apply(ok, 4, ok, ok, 4, 8, ok, ok, 4, None) == 1   # record below the header
+    assert lib.dsa_decode_queue_apply(ok, 64, ok, ok, 0, 8, ok, ok, 4, None) == 1  # no slots
+    assert lib.dsa_decode_queue_apply(ok, 64, ok, ok, 4, 8, ok, ok, 0, None) == 1  # no batch rows
