@@ -187,9 +187,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch-scale", type=float, default=1.0,
                     help="profiling only: run the config with its batch scaled down (ncu captures)")
-    ap.add_argument("--op", choices=["indexer", "cache_write", "sparse_attention"], default="indexer",
+    ap.add_argument("--op", choices=["indexer", "cache_write", "sparse_attention", "decode_loop"], default="indexer",
                     help="cache_write: the index-K cache writer (FP8 quantiser); sparse_attention: the "
-                         "consumer of topk_indices (sparse MLA attention over the selected slots)")
+                         "consumer of topk_indices (sparse MLA attention over the selected slots); "
+                         "decode_loop: a decode loop over --config's requests through the device work "
+                         "queue and through the per-step graph runner")
     ap.add_argument("--attn-tokens", type=int, default=128, help="sparse_attention: query tokens per step")
     ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
     ap.add_argument("--exchange", choices=["alltoall", "allgather"], default="alltoall",
@@ -210,6 +212,8 @@ def main():
         return cache_write_bench(args, rank, local)
     if args.op == "sparse_attention":
         return sparse_attention_bench(args, rank, local)
+    if args.op == "decode_loop":
+        return decode_loop_bench(args, rank, local)
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -589,6 +593,129 @@ def cache_write_bench(args, rank, local):
                          "frac": achieved / hbm, "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": algo, "kernel": "dsa::cache_write_kernel<true>"},
             "gpu_launches": args.steps, "clocks": clk.summary(), "cpu_baseline": cpu}), flush=True)
+
+
+def decode_loop_bench(args, rank, local):
+    """A decode loop over the requests of `--config` (1 or 2; default 2):
+    every step each request grows by one token, taking the next free page of
+    the pool when it crosses a page boundary, and the indexer runs over the
+    whole batch. q and weights are device tensors, as the model produces
+    them. Two host paths, the same device work:
+      graph_runner  every step copies seq_lens and the full block table from
+                    pinned host memory into the graph's buffers (double-
+                    buffered host arrays), then replays the indexer graph;
+      decode_queue  every step copies one record (the step's page appends and
+                    the batch list) and replays [apply + gather, indexer];
+                    the request table stays in device memory.
+    K steps timed as one span with CUDA events on the caller's stream (steps
+    not synchronised); config 2's K pages are far larger than L2, other
+    configs get the L2 flush between steps. Both paths end with bit-equal
+    outputs (checked). One process; rank 0 prints."""
+    import numpy as np
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    wl = importlib.import_module(PKG_NAME + ".workloads")
+    gr = importlib.import_module(PKG_NAME + ".graph_runner")
+    dqm = importlib.import_module(PKG_NAME + ".decode_queue")
+    cfg = 2 if args.config not in (1, 2) else args.config
+    w = wl.config(cfg, device=dev)
+    B, K, Wm = w.batch, args.steps, max(3, args.warmup)
+    total = Wm + K
+    sl0 = w.seq_lens.cpu().numpy().astype(np.int64)
+    bt0 = w.block_table.cpu().numpy()
+    np0 = (sl0 + 63) // 64
+    max_pages = int(max(bt0.shape[1], int((sl0 + total + 63).max()) // 64 + 1))
+    used = np.zeros(w.num_pages, dtype=bool)
+    for b in range(B):
+        used[bt0[b, :np0[b]]] = True
+    free = np.flatnonzero(~used).astype(np.int64)
+    flush = L2Flush(torch, dev) if cfg != 2 else (lambda: None)
+    cur = torch.cuda.current_stream(dev)
+
+    def appends(lens, npg):
+        """Rows whose next token needs a new page (each takes the next free page)."""
+        return np.flatnonzero(lens + 1 > 64 * npg)
+
+    # ---- graph runner: full seq_lens / block table from pinned host memory every step
+    runner = gr.GraphRunner(w.k_cache, max_batch=B, max_pages=max_pages, buckets=[B])
+    lens, npg, fp = sl0.copy(), np0.copy(), 0
+    host = []
+    for _ in range(2):
+        bt_h = torch.zeros((B, max_pages), dtype=torch.int32).pin_memory()
+        bt_h[:, :bt0.shape[1]] = torch.from_numpy(bt0)
+        host.append([bt_h, torch.zeros(B, dtype=torch.int32).pin_memory(), None])
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for i in range(total):
+        if i == Wm:
+            torch.cuda.synchronize()
+            ev[0].record(cur)
+            t0 = time.perf_counter()
+        bt_h, sl_h, done = host[i % 2]
+        if done is not None:
+            done.synchronize()
+        rows = appends(lens, npg)
+        # Both host copies get the new pages; the other copy may still be in
+        # flight for the previous step, which does not read these entries.
+        for h in host:
+            h[0][rows, npg[rows]] = torch.from_numpy(free[fp:fp + rows.size].astype(np.int32))
+        fp += rows.size
+        npg[rows] += 1
+        lens += 1
+        sl_h.copy_(torch.from_numpy(lens.astype(np.int32)))
+        flush()
+        out_a = runner(w.q, w.weights, sl_h, bt_h)
+        e = torch.cuda.Event()
+        e.record(runner.stream)
+        host[i % 2][2] = e
+    ev[1].record(cur)
+    torch.cuda.synchronize()
+    t_host_a = (time.perf_counter() - t0) / K
+    ms_a = ev[0].elapsed_time(ev[1]) / K
+    out_a = out_a.clone()
+    h2d_a = B * 4 + B * max_pages * 4
+
+    # ---- device work queue: one record per step, the request table on the device
+    dq = dqm.DecodeQueue(w.k_cache, num_slots=B, max_pages=max_pages, max_batch=B, buckets=[B],
+                         record_words=int(np0.sum()) + 8 * B + 64)
+    for b in range(B):
+        dq.admit(b, int(sl0[b]), bt0[b, :np0[b]])
+    slots = np.arange(B)
+    lens, npg, fp = sl0.copy(), np0.copy(), 0
+    rec_words = 0
+    for i in range(total):
+        if i == Wm:
+            torch.cuda.synchronize()
+            ev[0].record(cur)
+            t0 = time.perf_counter()
+        rows = appends(lens, npg)
+        for r, pid in zip(rows.tolist(), free[fp:fp + rows.size].tolist()):
+            dq.append_page(r, pid)
+        fp += rows.size
+        npg[rows] += 1
+        lens += 1
+        if i >= Wm:
+            rec_words += dq.table.record_words(B)
+        flush()
+        out_b = dq.step(slots, w.q, w.weights)
+    ev[1].record(cur)
+    torch.cuda.synchronize()
+    t_host_b = (time.perf_counter() - t0) / K
+    ms_b = ev[0].elapsed_time(ev[1]) / K
+    same = bool(torch.equal(out_b, out_a))
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode-loop queries/s (indexer step with its per-step host-to-device input transfer)",
+            "value": B / (ms_b * 1e-3), "unit": "queries/s", "n_gpus": 1, "steps": K, "warmup": Wm,
+            "ms_per_step": ms_b, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": w.name + " decode loop (+1 token per request per step)", "batch": B,
+                       "max_pages": max_pages, "l2": "K pages far larger than L2" if cfg == 2 else L2Flush.NOTE},
+            "decode_queue": {"ms_per_step": ms_b, "h2d_bytes_per_step": 4 * rec_words / K,
+                             "host_ms_per_step": t_host_b * 1e3},
+            "graph_runner": {"ms_per_step": ms_a, "value": B / (ms_a * 1e-3), "h2d_bytes_per_step": h2d_a,
+                             "host_ms_per_step": t_host_a * 1e3},
+            "outputs_equal": same, "gpu_launches": 3 * K}), flush=True)
 
 
 def sparse_attention_bench(args, rank, local):

@@ -47,12 +47,16 @@ class RequestTable:
     requests in use whose advanced length stays within their pages."""
 
     def __init__(self, num_slots, max_pages):
+        import numpy as np
         if num_slots < 1 or max_pages < 1:
             raise ValueError("num_slots and max_pages must be positive")
+        self.np = np
         self.num_slots, self.max_pages = int(num_slots), int(max_pages)
-        self.lens = [-1] * self.num_slots      # -1: slot free
+        self.lens = np.full(self.num_slots, -1, dtype=np.int64)  # -1: slot free
+        self.npages = np.zeros(self.num_slots, dtype=np.int64)
         self.pages = [[] for _ in range(self.num_slots)]
-        self.events = []                       # int32 words queued for the next record
+        self.events = []                                          # int32 words queued for the next record
+        self.n_events = 0
 
     def _slot(self, slot):
         slot = int(slot)
@@ -77,7 +81,8 @@ class RequestTable:
             raise ValueError(f"seq_len {seq_len} does not fit {len(pages)} pages")
         pad = (-len(pages)) % 4
         self.events += [DSA_QUEUE_ADMIT, slot, int(seq_len), len(pages)] + pages + [0] * pad
-        self.lens[slot], self.pages[slot] = int(seq_len), pages
+        self.n_events += 1
+        self.lens[slot], self.pages[slot], self.npages[slot] = int(seq_len), pages, len(pages)
 
     def append_page(self, slot, page_id):
         slot = self._in_use(slot)
@@ -85,54 +90,73 @@ class RequestTable:
         if idx >= self.max_pages:
             raise ValueError(f"slot {slot} already holds max_pages {self.max_pages} pages")
         self.events += [DSA_QUEUE_APPEND_PAGE, slot, idx, int(page_id)]
+        self.n_events += 1
         self.pages[slot].append(int(page_id))
+        self.npages[slot] = idx + 1
 
     def set_len(self, slot, seq_len):
         slot = self._in_use(slot)
         if not 0 <= int(seq_len) <= PAGE * len(self.pages[slot]):
             raise ValueError(f"seq_len {seq_len} does not fit the {len(self.pages[slot])} pages of slot {slot}")
         self.events += [DSA_QUEUE_SET_LEN, slot, int(seq_len), 0]
+        self.n_events += 1
         self.lens[slot] = int(seq_len)
 
     def retire(self, slot):
         slot = self._in_use(slot)
         self.events += [DSA_QUEUE_RETIRE, slot, 0, 0]
-        self.lens[slot], self.pages[slot] = -1, []
+        self.n_events += 1
+        self.lens[slot], self.pages[slot], self.npages[slot] = -1, [], 0
 
     def check_step(self, slots, advance):
-        """Raises if the step cannot run; leaves the mirror unchanged."""
-        slots = [self._in_use(s) for s in slots]
-        if len(set(slots)) != len(slots):
-            raise ValueError("a slot is listed twice in one step")
+        """Raises if the step cannot run; leaves the mirror unchanged.
+        Returns the slots as an int64 array."""
+        np = self.np
+        s = np.asarray(slots, dtype=np.int64).reshape(-1)
         if advance < 0:
             raise ValueError("advance must be >= 0")
-        for s in slots:
-            if self.lens[s] + advance > PAGE * len(self.pages[s]):
-                raise ValueError(f"slot {s}: length {self.lens[s] + advance} needs a page it has not been given")
-        return slots
+        last = getattr(self, "_distinct", None)
+        if last is None or last.shape != s.shape or not np.array_equal(last, s):
+            # a decode loop usually lists the same slots step after step:
+            # range and uniqueness are checked once per distinct list
+            if s.size and (s.min() < 0 or s.max() >= self.num_slots):
+                raise ValueError(f"a slot lies outside [0, {self.num_slots})")
+            if np.unique(s).size != s.size:
+                raise ValueError("a slot is listed twice in one step")
+            self._distinct = s.copy()
+        ln = self.lens[s]
+        if (ln < 0).any():
+            raise ValueError(f"slot {int(s[np.argmax(ln < 0)])} holds no request")
+        over = ln + advance > PAGE * self.npages[s]
+        if over.any():
+            b = int(np.argmax(over))
+            raise ValueError(f"slot {int(s[b])}: length {int(ln[b]) + advance} needs a page it has not been given")
+        return s
 
-    def build_record(self, slots, advance=1):
-        """The step's record (list of int32 words); applies the advance to
-        the mirror and clears the queued events."""
-        slots = self.check_step(slots, advance)
-        ev = self.events
-        n_events = 0
-        i = 0
-        while i < len(ev):  # count events (an admission carries its padded page list)
-            n_events += 1
-            i += 4 + ((ev[i + 3] + 3) // 4 * 4 if ev[i] == DSA_QUEUE_ADMIT else 0)
-        batch_off = DSA_QUEUE_HEADER_WORDS + len(ev)
-        words = batch_off + len(slots)
-        rec = [words, n_events, len(slots), int(advance), batch_off, 0, 0, 0] + ev + slots
-        for s in slots:
-            self.lens[s] += int(advance)
-        self.events = []
+    def record_words(self, batch):
+        """Words of the next record for a batch of `batch` rows."""
+        return DSA_QUEUE_HEADER_WORDS + len(self.events) + int(batch)
+
+    def build_record(self, slots, advance=1, checked=False):
+        """The step's record (int32 numpy array); applies the advance to the
+        mirror and clears the queued events. `checked`: `slots` is the array
+        check_step returned for this advance (skips a second check)."""
+        np = self.np
+        s = slots if checked else self.check_step(slots, advance)
+        batch_off = DSA_QUEUE_HEADER_WORDS + len(self.events)
+        words = batch_off + s.size
+        rec = np.empty(words, dtype=np.int32)
+        rec[:DSA_QUEUE_HEADER_WORDS] = [words, self.n_events, s.size, int(advance), batch_off, 0, 0, 0]
+        rec[DSA_QUEUE_HEADER_WORDS:batch_off] = self.events
+        rec[batch_off:] = s
+        self.lens[s] += int(advance)
+        self.events, self.n_events = [], 0
         return rec
 
     def batch_inputs(self, slots):
         """(seq_lens [B], block_table [B, max_pages]) of the listed requests
         as the mirror holds them (zeros past each row's pages), as numpy."""
-        import numpy as np
+        np = self.np
         sl = np.array([self.lens[s] for s in slots], dtype=np.int32)
         bt = np.zeros((len(slots), self.max_pages), dtype=np.int32)
         for b, s in enumerate(slots):
@@ -172,7 +196,8 @@ class DecodeQueue:
         self.idle_record[0] = DSA_QUEUE_HEADER_WORDS
         self.idle_record[4] = DSA_QUEUE_HEADER_WORDS
         self.pinned = [torch.zeros(self.record_words, dtype=i32).pin_memory() for _ in range(int(ring))]
-        self.copied = [None] * int(ring)
+        self.pinned_np = [t.numpy() for t in self.pinned]
+        self.copied = [torch.cuda.Event() for _ in range(int(ring))]  # last copy out of each pinned buffer
         self.next_ring = 0
         self.graphs = {}
 
@@ -216,39 +241,46 @@ class DecodeQueue:
         self.graphs[size] = (g, bufs)
         return self.graphs[size]
 
+    def input_buffers(self, batch):
+        """(q [batch, 64, 128] e4m3, weights [batch, 64] fp32) views of the
+        graph buffers a step of `batch` rows reads: a producer that writes
+        its outputs there saves step() the two copies."""
+        size = bucket_for(batch, self.sizes)
+        _, bufs = self.graphs.get(size) or self._capture(size)
+        return bufs["q"][:batch], bufs["w"][:batch]
+
     def step(self, slots, q, weights, advance=1):
         """One decode step over the requests in `slots` (batch order): their
         lengths grow by `advance`, then the indexer runs with q [B, 64, 128]
-        e4m3 and weights [B, 64] fp32 (device or pinned host tensors).
+        e4m3 and weights [B, 64] fp32 (device or pinned host tensors, or the
+        views input_buffers(B) returned, which are used in place).
         Returns the [B, 2048] top-K slots (a view, see the class docstring)."""
         torch = self.torch
-        slots = [int(s) for s in slots]
         B = len(slots)
         if B == 0:
             raise ValueError("empty step")
         if tuple(q.shape) != (B, HEADS, DIM) or tuple(weights.shape) != (B, HEADS):
             raise ValueError("q must be [B, 64, 128] and weights [B, 64] for the B listed slots")
         size = bucket_for(B, self.sizes)
-        self.table.check_step(slots, advance)
-        n = DSA_QUEUE_HEADER_WORDS + len(self.table.events) + B
+        s = self.table.check_step(slots, advance)
+        n = self.table.record_words(B)
         if n > self.record_words:
             raise ValueError(f"step record of {n} words exceeds record_words {self.record_words}")
         g, bufs = self.graphs.get(size) or self._capture(size)
-        rec = self.table.build_record(slots, advance)
+        rec = self.table.build_record(s, advance, checked=True)
         j = self.next_ring
         self.next_ring = (j + 1) % len(self.pinned)
-        if self.copied[j] is not None:
-            self.copied[j].synchronize()  # the copy that last read this pinned buffer has finished
-        self.pinned[j][:n] = torch.tensor(rec, dtype=torch.int32)
+        self.copied[j].synchronize()  # the copy that last read this pinned buffer has finished
+        self.pinned_np[j][:n] = rec
         cur = torch.cuda.current_stream(self.dev)
         self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
             self.record[:n].copy_(self.pinned[j][:n], non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(self.stream)
-            self.copied[j] = ev
-            bufs["q"][:B].copy_(q, non_blocking=True)
-            bufs["w"][:B].copy_(weights, non_blocking=True)
+            self.copied[j].record(self.stream)
+            if q.data_ptr() != bufs["q"].data_ptr():
+                bufs["q"][:B].copy_(q, non_blocking=True)
+            if weights.data_ptr() != bufs["w"].data_ptr():
+                bufs["w"][:B].copy_(weights, non_blocking=True)
             g.replay()
         cur.wait_stream(self.stream)
         return bufs["out"][:B]

@@ -120,7 +120,7 @@ def test_record_encoding_matches_model():
     rng = np.random.default_rng(3)
     n_steps = 0
     for rec, slots in _script(t, rng, list(range(3000)), 60, 8):
-        sl, rows, bad = apply_model(rec, req_len, req_bt, 8)
+        sl, rows, bad = apply_model([int(x) for x in rec], req_len, req_bt, 8)
         assert not bad
         ref_sl, ref_bt = t.batch_inputs(slots)
         assert list(sl[:len(slots)]) == list(ref_sl) and not sl[len(slots):].any()
@@ -156,7 +156,7 @@ def test_request_table_rejects_bad_changes():
     with pytest.raises(ValueError):
         t.append_page(0, 11)                # past max_pages
     rec = t.build_record([0], 1)
-    assert rec[1] == 3 and rec[2] == 1 and rec[rec[4]] == 0  # admit + two appends; batch [0]
+    assert rec[1] == 3 and rec[2] == 1 and rec[rec[4]] == 0 and len(rec) == rec[0]  # admit + two appends
     assert t.lens[0] == 65
     t.retire(0)
     with pytest.raises(ValueError):
@@ -217,7 +217,13 @@ def test_queue_steps_equal_direct_calls():
         B = len(slots)
         q = (torch.randn((B, 64, 128), generator=g, device="cuda") * 0.5).to(torch.float8_e4m3fn)
         w = torch.rand((B, 64), generator=g, device="cuda") / 8
-        got = dq.step(slots, q, w).clone()
+        if it % 2:
+            got = dq.step(slots, q, w).clone()
+        else:  # the producer writes straight into the graph's input buffers
+            qb, wb = dq.input_buffers(B)
+            qb.copy_(q)
+            wb.copy_(w)
+            got = dq.step(slots, qb, wb).clone()
         sl, bt = table.batch_inputs(slots)  # the mirror after this step's advance
         ref = torch.empty((B, 2048), dtype=torch.int32, device="cuda")
         pkg.launch_topk_c(q, kc, w, torch.from_numpy(sl).cuda(), torch.from_numpy(bt).cuda(), ref)
