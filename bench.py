@@ -477,6 +477,10 @@ def main():
     if rank == 0:
         kernel = (DOMINANT_PARTIAL.get(path, path) + " (partial, key range)") if key_sharded else DOMINANT.get(path, path)
         tr = traffic_per_launch(args.config, kernel)
+        if tr is not None and not key_sharded and args.config not in PREFILL_CONFIGS and kbytes != global_kbytes:
+            # The table holds the whole batch's launch; a rank's launch moves its
+            # share (DRAM traffic grows with the K bytes a launch reads).
+            tr = int(round(tr * kbytes / global_kbytes))
         if args.config in PREFILL_CONFIGS:
             # K is L2-resident (one sequence): the contraction on the tensor
             # cores bounds the kernel. B200's dense fp8 rate is twice bf16.
