@@ -58,7 +58,7 @@ constexpr int kPTmemCols = 4 * kPBufCols;          // (parity, pair) buffers: al
 
 // Shared memory map (byte offsets from a 1024-aligned base).
 constexpr int kPOffK = 0;                                  // kPStages x 16384, swizzled K tiles
-constexpr int kPOffQ = kPOffK + kPStages * 16384;          // kPQ x 8192, swizzled Q (N = 256 rows)
+constexpr int kPOffQ = kPOffK + kPStages * 16384;          // kPQ x 8192, swizzled Q (4 x 64 head rows)
 constexpr int kPOffCand = kPOffQ + kPQ * 8192;             // kPQ x kPCap x 8
 constexpr int kPOffHist = kPOffCand + kPQ * kPCap * 8;     // kPQ x 256 x 4
 constexpr int kPOffW = kPOffHist + kPQ * 256 * 4;          // kPQ x 64 x 4

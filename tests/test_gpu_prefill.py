@@ -2,7 +2,7 @@
 
 Batches of 256 rows or more first go through the shared-sequence kernel,
 which serves every group of four consecutive rows whose block-table entries
-agree over their visible keys (one K stream, one N = 256 MMA per tile) and
+agree over their visible keys (one K stream and one N = 128 MMA per row pair and tile) and
 leaves the other rows to the per-row kernel. These tests mix both kinds of
 group in one batch, including groups that agree on every page but the last
 visible one, and batches whose size is not a multiple of four.
