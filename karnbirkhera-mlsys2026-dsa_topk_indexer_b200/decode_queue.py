@@ -55,8 +55,12 @@ class RequestTable:
         self.lens = np.full(self.num_slots, -1, dtype=np.int64)  # -1: slot free
         self.npages = np.zeros(self.num_slots, dtype=np.int64)
         self.pages = [[] for _ in range(self.num_slots)]
-        self.events = []                                          # int32 words queued for the next record
-        self.n_events = 0
+        self.events = []      # events queued for the next record, each a list of int32 words
+        self.event_words = 0  # their total words
+
+    def _queue(self, words):
+        self.events.append(words)
+        self.event_words += len(words)
 
     def _slot(self, slot):
         slot = int(slot)
@@ -80,8 +84,7 @@ class RequestTable:
         if not 0 <= int(seq_len) <= PAGE * len(pages):
             raise ValueError(f"seq_len {seq_len} does not fit {len(pages)} pages")
         pad = (-len(pages)) % 4
-        self.events += [DSA_QUEUE_ADMIT, slot, int(seq_len), len(pages)] + pages + [0] * pad
-        self.n_events += 1
+        self._queue([DSA_QUEUE_ADMIT, slot, int(seq_len), len(pages)] + pages + [0] * pad)
         self.lens[slot], self.pages[slot], self.npages[slot] = int(seq_len), pages, len(pages)
 
     def append_page(self, slot, page_id):
@@ -89,8 +92,7 @@ class RequestTable:
         idx = len(self.pages[slot])
         if idx >= self.max_pages:
             raise ValueError(f"slot {slot} already holds max_pages {self.max_pages} pages")
-        self.events += [DSA_QUEUE_APPEND_PAGE, slot, idx, int(page_id)]
-        self.n_events += 1
+        self._queue([DSA_QUEUE_APPEND_PAGE, slot, idx, int(page_id)])
         self.pages[slot].append(int(page_id))
         self.npages[slot] = idx + 1
 
@@ -98,14 +100,12 @@ class RequestTable:
         slot = self._in_use(slot)
         if not 0 <= int(seq_len) <= PAGE * len(self.pages[slot]):
             raise ValueError(f"seq_len {seq_len} does not fit the {len(self.pages[slot])} pages of slot {slot}")
-        self.events += [DSA_QUEUE_SET_LEN, slot, int(seq_len), 0]
-        self.n_events += 1
+        self._queue([DSA_QUEUE_SET_LEN, slot, int(seq_len), 0])
         self.lens[slot] = int(seq_len)
 
     def retire(self, slot):
         slot = self._in_use(slot)
-        self.events += [DSA_QUEUE_RETIRE, slot, 0, 0]
-        self.n_events += 1
+        self._queue([DSA_QUEUE_RETIRE, slot, 0, 0])
         self.lens[slot], self.pages[slot], self.npages[slot] = -1, [], 0
 
     def check_step(self, slots, advance):
@@ -135,7 +135,28 @@ class RequestTable:
 
     def record_words(self, batch):
         """Words of the next record for a batch of `batch` rows."""
-        return DSA_QUEUE_HEADER_WORDS + len(self.events) + int(batch)
+        return DSA_QUEUE_HEADER_WORDS + self.event_words + int(batch)
+
+    def take_events(self, max_words):
+        """A record with no batch rows that carries the oldest queued events
+        fitting in `max_words` words (at least one event), removing them from
+        the queue; None when nothing is queued. Lets a burst of changes
+        larger than one record go ahead of the step in several records."""
+        np = self.np
+        if not self.events:
+            return None
+        n, words = 0, DSA_QUEUE_HEADER_WORDS
+        while n < len(self.events) and (n == 0 or words + len(self.events[n]) <= max_words):
+            words += len(self.events[n])
+            n += 1
+        if words > max_words:
+            raise ValueError(f"one event of {words - DSA_QUEUE_HEADER_WORDS} words exceeds a record")
+        rec = np.empty(words, dtype=np.int32)
+        rec[:DSA_QUEUE_HEADER_WORDS] = [words, n, 0, 0, words, 0, 0, 0]
+        rec[DSA_QUEUE_HEADER_WORDS:] = [w for ev in self.events[:n] for w in ev]
+        self.events = self.events[n:]
+        self.event_words -= words - DSA_QUEUE_HEADER_WORDS
+        return rec
 
     def build_record(self, slots, advance=1, checked=False):
         """The step's record (int32 numpy array); applies the advance to the
@@ -143,14 +164,15 @@ class RequestTable:
         check_step returned for this advance (skips a second check)."""
         np = self.np
         s = slots if checked else self.check_step(slots, advance)
-        batch_off = DSA_QUEUE_HEADER_WORDS + len(self.events)
+        batch_off = DSA_QUEUE_HEADER_WORDS + self.event_words
         words = batch_off + s.size
         rec = np.empty(words, dtype=np.int32)
-        rec[:DSA_QUEUE_HEADER_WORDS] = [words, self.n_events, s.size, int(advance), batch_off, 0, 0, 0]
-        rec[DSA_QUEUE_HEADER_WORDS:batch_off] = self.events
+        rec[:DSA_QUEUE_HEADER_WORDS] = [words, len(self.events), s.size, int(advance), batch_off, 0, 0, 0]
+        if self.events:
+            rec[DSA_QUEUE_HEADER_WORDS:batch_off] = [w for ev in self.events for w in ev]
         rec[batch_off:] = s
         self.lens[s] += int(advance)
-        self.events, self.n_events = [], 0
+        self.events, self.event_words = [], 0
         return rec
 
     def batch_inputs(self, slots):
@@ -170,9 +192,11 @@ class DecodeQueue:
     k_cache [num_pages, 64, 1, 132] is the serving system's paged index-K
     cache, fixed for the runner's life (it is captured into the graphs).
     Records are staged through a ring of `ring` pinned host buffers of
-    `record_words` int32 words; a step whose record is larger raises
-    (admit fewer requests per step). `step` returns a view of the bucket's
-    output rows, valid until the next step that uses the same bucket."""
+    `record_words` int32 words; when the changes queued since the last step
+    do not fit in one record with the batch list, the oldest go ahead in
+    records of their own (applied outside the graph, on the runner's stream,
+    before the step). `step` returns a view of the bucket's output rows,
+    valid until the next step that uses the same bucket."""
 
     def __init__(self, k_cache, num_slots, max_pages, max_batch, record_words=1 << 18, buckets=None, ring=4,
                  stream=None):
@@ -202,9 +226,6 @@ class DecodeQueue:
         self.graphs = {}
 
     # request bookkeeping (queued, sent with the next step's record)
-    def admit(self, slot, seq_len, pages):
-        self.table.admit(slot, seq_len, pages)
-
     def append_page(self, slot, page_id):
         self.table.append_page(slot, page_id)
 
@@ -263,20 +284,15 @@ class DecodeQueue:
             raise ValueError("q must be [B, 64, 128] and weights [B, 64] for the B listed slots")
         size = bucket_for(B, self.sizes)
         s = self.table.check_step(slots, advance)
-        n = self.table.record_words(B)
-        if n > self.record_words:
-            raise ValueError(f"step record of {n} words exceeds record_words {self.record_words}")
         g, bufs = self.graphs.get(size) or self._capture(size)
-        rec = self.table.build_record(s, advance, checked=True)
-        j = self.next_ring
-        self.next_ring = (j + 1) % len(self.pinned)
-        self.copied[j].synchronize()  # the copy that last read this pinned buffer has finished
-        self.pinned_np[j][:n] = rec
         cur = torch.cuda.current_stream(self.dev)
         self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
-            self.record[:n].copy_(self.pinned[j][:n], non_blocking=True)
-            self.copied[j].record(self.stream)
+            while self.table.record_words(B) > self.record_words:  # a burst of changes: send the oldest first
+                rec = self.table.take_events(self.record_words)
+                self._send(rec)
+                self.pkg.decode_queue_apply(self.record, self.req_len, self.req_bt, bufs["sl"], bufs["bt"])
+            self._send(self.table.build_record(s, advance, checked=True))
             if q.data_ptr() != bufs["q"].data_ptr():
                 bufs["q"][:B].copy_(q, non_blocking=True)
             if weights.data_ptr() != bufs["w"].data_ptr():
@@ -284,6 +300,23 @@ class DecodeQueue:
             g.replay()
         cur.wait_stream(self.stream)
         return bufs["out"][:B]
+
+    def _send(self, rec):
+        """Copies one record into the device record buffer (on the current
+        stream) through the next pinned ring buffer."""
+        n = rec.size
+        j = self.next_ring
+        self.next_ring = (j + 1) % len(self.pinned)
+        self.copied[j].synchronize()  # the copy that last read this pinned buffer has finished
+        self.pinned_np[j][:n] = rec
+        self.record[:n].copy_(self.pinned[j][:n], non_blocking=True)
+        self.copied[j].record(self.torch.cuda.current_stream(self.dev))
+
+    def admit(self, slot, seq_len, pages):
+        pages = list(pages)
+        if DSA_QUEUE_HEADER_WORDS + 4 + len(pages) + 3 > self.record_words:
+            raise ValueError(f"an admission of {len(pages)} pages does not fit a record of {self.record_words} words")
+        self.table.admit(slot, seq_len, pages)
 
     def device_table(self):
         """(req_len, req_block_table) as the device holds them (synchronises)."""

@@ -133,6 +133,40 @@ def test_record_encoding_matches_model():
     assert n_steps > 30
 
 
+def test_event_bursts_split_into_records():
+    """Queued changes larger than one record go out as batch-less records of
+    whole events (oldest first), then the step's record; applied in order
+    they give the same table as one large record."""
+    m = _mod()
+    t = m.RequestTable(num_slots=8, max_pages=40)
+    req_len = np.full(8, -1, dtype=np.int64)
+    req_bt = np.zeros((8, 40), dtype=np.int64)
+    for s in range(6):
+        t.admit(s, 64 * (5 + s) - 7, list(range(100 * s, 100 * s + 5 + s)))
+    t.retire(2)
+    t.append_page(3, 999)
+    cap = 48
+    recs = []
+    while t.record_words(4) > cap:
+        r = t.take_events(cap)
+        assert r[2] == 0 and len(r) <= cap
+        recs.append(r)
+    recs.append(t.build_record([0, 1, 3, 5], 1))
+    assert len(recs) > 2 and len(recs[-1]) <= cap and t.events == []
+    for r in recs:
+        sl, rows, bad = apply_model([int(x) for x in r], req_len, req_bt, 4)
+        assert not bad
+    ref_sl, ref_bt = t.batch_inputs([0, 1, 3, 5])
+    assert list(sl) == list(ref_sl)
+    for b in range(4):
+        assert list(rows[b]) == list(ref_bt[b, :len(rows[b])])
+    for s in range(8):
+        assert req_len[s] == t.lens[s]
+    with pytest.raises(ValueError):
+        t.admit(6, 10, list(range(40)))
+        t.take_events(20)  # one admission of 40 pages cannot fit 20 words
+
+
 def test_request_table_rejects_bad_changes():
     m = _mod()
     t = m.RequestTable(num_slots=4, max_pages=3)
@@ -236,6 +270,34 @@ def test_queue_steps_equal_direct_calls():
     for s in range(24):
         assert int(req_len[s]) == table.lens[s]
         assert req_bt[s, :len(table.pages[s])].tolist() == table.pages[s]
+
+
+@pytest.mark.gpu
+def test_queue_bursts_larger_than_a_record():
+    """Admissions of many pages with a small record buffer: the queue sends
+    them in several records before the step; results equal direct calls."""
+    pkg = package()
+    m = _mod()
+    kc = _queue_setup(n_pages=400, seed=12)
+    dq = m.DecodeQueue(kc, num_slots=8, max_pages=64, max_batch=8, buckets=[8], record_words=96)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    pages = torch.randperm(400, generator=torch.Generator().manual_seed(3)).tolist()
+    for s in range(8):
+        n = 20 + 5 * s
+        dq.admit(s, 64 * n - 3 * s - 1, pages[:n])
+        pages = pages[n:]
+    for step in range(3):
+        slots = [7, 0, 3, 5, 1] if step != 1 else [2, 4, 6]
+        B = len(slots)
+        q = (torch.randn((B, 64, 128), generator=g, device="cuda") * 0.5).to(torch.float8_e4m3fn)
+        w = torch.rand((B, 64), generator=g, device="cuda") / 8
+        got = dq.step(slots, q, w, advance=0).clone()
+        sl, bt = dq.table.batch_inputs(slots)
+        ref = torch.empty((B, 2048), dtype=torch.int32, device="cuda")
+        pkg.launch_topk_c(q, kc, w, torch.from_numpy(sl).cuda(), torch.from_numpy(bt).cuda(), ref)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), step
+    assert pkg.device_status(0) == 0
 
 
 @pytest.mark.gpu
