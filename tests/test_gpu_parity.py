@@ -348,3 +348,47 @@ def test_cluster_kernel_path(pkg, cfg, monkeypatch):
         w = _rows(w, list(range(0, 8192, 37)))
     assert_parity(pkg, w)
     assert pkg.last_path() == "cluster"
+
+
+def _schedules(pkg, w, settings, monkeypatch):
+    """Output of the same batch under each setting (a dict of switches)."""
+    outs = []
+    for env in settings:
+        for k in ("DSA_TOPK_CLUSTER", "DSA_TOPK_SPLIT", "DSA_TOPK_TAIL", "DSA_TOPK_PREFILL"):
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        outs.append((env, run(pkg, w), pkg.last_path()))
+    return outs
+
+
+def test_schedules_bit_identical_decode(pkg, monkeypatch):
+    """Every key's score comes from one routine and the selection is exact,
+    so the decode schedules agree bit for bit: cluster sizes 1 to 8, the
+    two-class split and the last-wave launch on and off."""
+    g = torch.Generator().manual_seed(71)
+    u = torch.rand(160, generator=g, dtype=torch.float64)
+    sl = torch.exp(np.log(300) + u * (np.log(40000) - np.log(300))).floor().to(torch.int32)
+    sl[:5] = torch.tensor([0, 1, 2047, 2048, 2049], dtype=torch.int32)
+    w = workloads().custom(sl.tolist(), seed=72)
+    settings = [{}, {"DSA_TOPK_SPLIT": "0", "DSA_TOPK_TAIL": "0"}, {"DSA_TOPK_TAIL": "0"}] + \
+               [{"DSA_TOPK_CLUSTER": str(c)} for c in (1, 2, 3, 4, 8)]
+    outs = _schedules(pkg, w, settings, monkeypatch)
+    base = outs[0][1]
+    for env, o, path in outs[1:]:
+        assert np.array_equal(o, base), (env, path)
+    assert len({p for _, _, p in outs}) >= 2  # more than one schedule really ran
+    assert_parity(pkg, w, base)
+
+
+def test_schedules_bit_identical_prefill(pkg, monkeypatch):
+    """The shared-sequence kernel and the per-row kernel (at two cluster
+    sizes) agree bit for bit on a causal batch."""
+    w = workloads().make_shared("xpath", 260, 12000, 200, 73)
+    settings = [{"DSA_TOPK_PREFILL": "1"}, {"DSA_TOPK_PREFILL": "0"},
+                {"DSA_TOPK_PREFILL": "0", "DSA_TOPK_CLUSTER": "4"}]
+    outs = _schedules(pkg, w, settings, monkeypatch)
+    assert outs[0][2] == "prefill+cluster" and outs[1][2] != "prefill+cluster"
+    for env, o, path in outs[1:]:
+        assert np.array_equal(o, outs[0][1]), (env, path)
+    assert_parity(pkg, w, outs[0][1])
