@@ -194,7 +194,7 @@ def main():
                          "queue and through the per-step graph runner")
     ap.add_argument("--attn-tokens", type=int, default=128, help="sparse_attention: query tokens per step")
     ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
-    ap.add_argument("--exchange", choices=["alltoall", "allgather"], default="alltoall",
+    ap.add_argument("--exchange", choices=["alltoall", "allgather", "peer"], default="alltoall",
                     help="key-sharded configs at N>1: how the per-rank candidate lists meet")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -237,6 +237,7 @@ def main():
     flush = L2Flush(torch, dev)
     stream = torch.cuda.current_stream(dev)
 
+    peer_ex = None
     if key_sharded:
         sh = importlib.import_module(PKG_NAME + ".sharding")
         counts = {}
@@ -254,8 +255,17 @@ def main():
             counts["m"] = pkg.last_launch_count()
             return r
 
+        # exchange="peer": candidate lists exchanged and merged over NVLink
+        # peer memory by the library's own kernels (no NCCL on the data path).
+        peer_ex = sh.PeerExchange(B, dev) if args.exchange == "peer" and world > 1 else None
+
         def run_sharded(q, kc, wt, sl, bt):
-            out.copy_(sh.key_sharded_topk(q, kc, wt, sl, bt, partial_fn=pfn, merge_fn=mfn, exchange=args.exchange))
+            out.copy_(sh.key_sharded_topk(q, kc, wt, sl, bt, partial_fn=pfn, merge_fn=mfn,
+                                          exchange=args.exchange if peer_ex else
+                                          ("alltoall" if args.exchange == "peer" else args.exchange),
+                                          peer=peer_ex))
+            if peer_ex is not None:
+                counts["m"] = pkg.last_launch_count()
             return counts["p"] + counts["m"]
 
         def call():
@@ -515,7 +525,10 @@ def main():
                        "global_kcache_bytes": global_kbytes,
                        "max_pages": w.max_pages,
                        "pool_pages": w.num_pages,
-                       "parallelism": (f"key-sharded x{world} (NCCL all-to-all of candidate lists, merge, all-gather "
+                       "parallelism": (f"key-sharded x{world} (candidate lists read over NVLink peer memory by a "
+                                       "fused merge kernel that stores each row into every rank; no NCCL on the "
+                                       "data path)" if args.exchange == "peer" else
+                                       f"key-sharded x{world} (NCCL all-to-all of candidate lists, merge, all-gather "
                                        "of results)" if args.exchange == "alltoall" else
                                        f"key-sharded x{world} (NCCL all-gather of candidate lists + merge)")
                        if key_sharded
@@ -535,6 +548,8 @@ def main():
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     del graph
+    if peer_ex is not None:
+        peer_ex.close()  # every rank together, before the group goes away
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -16,6 +16,7 @@
  *   - dsa_sparse_attention_launch: per-(device, stream) split buffers and
  *     counters, allocated the first time a shape needs them (outside capture).
  *   - dsa_topk_indexer_launch_noalloc allocates nothing (see below).
+ *   - dsa_peer_alloc allocates the peer-exchange region it is asked for.
  *   The other entry points allocate no device memory.
  *
  * Layouts (the reference operator dsa_topk_indexer_fp8_h64_d128_topk2048_ps64):
@@ -170,6 +171,45 @@ DSA_API int dsa_sparse_attention_launch(const void* q_nope, const void* q_pe, co
                                         const void* kpe_cache, const int32_t* sparse_indices, float sm_scale,
                                         void* output, float* lse, int64_t num_tokens, int64_t num_indices,
                                         int64_t num_pages, void* stream);
+
+/* Key-axis sharding over NVLink peer memory, without a collective library
+ * (the exchange and merge that dsa_topk_indexer_partial / _merge and NCCL
+ * otherwise do). Each rank allocates one region of dsa_peer_region_bytes(B)
+ * bytes with dsa_peer_alloc (cudaMalloc, zeroed; `ipc_handle` receives its
+ * 64-byte CUDA IPC handle), hands the handle to every other rank, and opens
+ * theirs with dsa_peer_open. Region layout, L = B*2048*4 bytes:
+ *   [0, L) cand_scores [B,2048] fp32 | [L, 2L) cand_pos [B,2048] int32 |
+ *   [2L, 3L) out [B,2048] int32 | then ready flags [64] and done flags [64]
+ *   (uint32 step counters, one per rank).
+ * Per step each rank writes its key range's best-first lists into its own
+ * cand_scores / cand_pos (dsa_topk_indexer_partial with those pointers), then
+ * calls dsa_peer_merge with `bases` = a DEVICE array [nranks] of every rank's
+ * region address as this rank maps it (its own allocation, the peers' opened
+ * addresses) and the same `epoch` on every rank, increasing by one per step
+ * (first step 1). Phases (bit mask, 15 = all, in this order on `stream`):
+ *   1 signal ready: ready[rank] = epoch in every region;
+ *   2 merge: CTA per row of rows [B*rank/nranks, B*(rank+1)/nranks): wait
+ *     until ready[0..nranks) = epoch in this rank's region, merge the lists of
+ *     every rank (peer loads), translate through block_table [B, max_pages]
+ *     and store the row into every rank's out (peer stores);
+ *   4 signal done: done[rank] = epoch in every region;
+ *   8 wait done: until done[0..nranks) = epoch in this rank's region; then
+ *     out holds all B rows, and no peer reads this rank's lists any more.
+ * Waits give up after wait_ns (0: 2 s) and raise DSA_STATUS_WAIT_TIMEOUT
+ * (the CTA that gave up writes nothing). At most 64 ranks. Plain peer loads
+ * and stores, no multicast. Results equal dsa_topk_indexer_merge over the
+ * same lists bit for bit. The reference has no multi-GPU path; this is the
+ * exchange its north star names (candidate lists gathered over NVLink, then
+ * a GPU merge), fused into one kernel. dsa_peer_alloc allocates (its purpose);
+ * call it outside stream capture. */
+DSA_API int dsa_peer_region_bytes(int64_t batch, int64_t* bytes);
+DSA_API int dsa_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+DSA_API int dsa_peer_open(const void* ipc_handle, void** ptr);
+DSA_API int dsa_peer_close(void* ptr);
+DSA_API int dsa_peer_free(void* ptr);
+DSA_API int dsa_peer_merge(const uint64_t* bases, int32_t nranks, int32_t rank, uint32_t epoch, int64_t batch,
+                           const int32_t* block_table, int64_t max_pages, int32_t phases, int64_t wait_ns,
+                           void* stream);
 
 /* Device work queue across decode steps. The request table stays in device
  * memory between steps: req_len [num_slots] int32 (-1 = slot not in use)

@@ -40,6 +40,12 @@ SIGNATURES = [
     ("dsa_topk_indexer_last_launch_count", _I32, []),
     ("dsa_topk_indexer_last_path", ctypes.c_char_p, []),
     ("dsa_index_cache_write", _I32, [_P, _I32, _P, _P, _I64, _I64, _P]),
+    ("dsa_peer_region_bytes", _I32, [_I64, ctypes.POINTER(ctypes.c_int64)]),
+    ("dsa_peer_alloc", _I32, [_I64, ctypes.POINTER(ctypes.c_void_p), _P]),
+    ("dsa_peer_open", _I32, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    ("dsa_peer_close", _I32, [_P]),
+    ("dsa_peer_free", _I32, [_P]),
+    ("dsa_peer_merge", _I32, [_P, _I32, _I32, ctypes.c_uint32, _I64, _P, _I64, _I32, _I64, _P]),
     ("dsa_decode_queue_apply", _I32, [_P, _I64, _P, _P, _I64, _I64, _P, _P, _I64, _P]),
     ("dsa_sparse_attention_launch", _I32, [_P, _P, _P, _P, _P, ctypes.c_float, _P, _P, _I64, _I64, _I64, _P]),
     ("dsa_topk_indexer_set_timing", _I32, [_I32]),

@@ -558,6 +558,8 @@ IndexerParams base_params(const void* kcache, const float* w, const int32_t* sl,
 }  // namespace
 }  // namespace dsa
 
+#include "peer_merge.cuh"  // uses load_list / merge_top above
+
 using namespace dsa;
 
 extern "C" int dsa_topk_indexer_launch(const void* q, const void* k_cache, const float* weights,
@@ -811,6 +813,94 @@ extern "C" int dsa_index_cache_write(const void* k, int k_dtype, const int64_t* 
         k, slots, static_cast<uint8_t*>(k_cache), num_tokens, num_pages);
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   t_last_launches = 1;
+  return DSA_OK;
+}
+
+// ------------------------------------------------- key-axis peer exchange
+extern "C" int dsa_peer_region_bytes(int64_t batch, int64_t* bytes) {
+  if (batch < 1 || batch > INT32_MAX || !bytes) return DSA_ERR_INVALID_ARG;
+  *bytes = PeerLayout{batch * kTopK * 4}.total();
+  return DSA_OK;
+}
+
+extern "C" int dsa_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+  if (bytes < 1 || !ptr || !ipc_handle) return DSA_ERR_INVALID_ARG;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  void* p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(bytes)) != cudaSuccess) return DSA_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, static_cast<size_t>(bytes)) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return DSA_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return DSA_OK;
+}
+
+extern "C" int dsa_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return DSA_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+extern "C" int dsa_peer_close(void* ptr) {
+  if (!ptr) return DSA_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+extern "C" int dsa_peer_free(void* ptr) {
+  if (!ptr) return DSA_ERR_INVALID_ARG;
+  return cudaFree(ptr) == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+extern "C" int dsa_peer_merge(const uint64_t* bases, int32_t nranks, int32_t rank, uint32_t epoch, int64_t batch,
+                              const int32_t* block_table, int64_t max_pages, int32_t phases, int64_t wait_ns,
+                              void* stream) {
+  t_last_launches = 0;
+  t_timed = false;
+  if (!bases || !block_table || nranks < 1 || nranks > kPeerMaxRanks || rank < 0 || rank >= nranks ||
+      batch < 1 || batch > INT32_MAX || max_pages < 1 || max_pages > INT32_MAX / kPage || (phases & ~15) != 0 ||
+      wait_ns < 0)
+    return DSA_ERR_INVALID_ARG;
+  int num_sms = 0;
+  int rc = prepare_device(&num_sms);
+  if (rc != DSA_OK) return rc;
+  PeerParams p{};
+  p.bases = bases;
+  p.nranks = nranks;
+  p.rank = rank;
+  p.epoch = epoch;
+  p.lay = PeerLayout{batch * kTopK * 4};
+  p.batch = static_cast<int32_t>(batch);
+  p.max_pages = static_cast<int32_t>(max_pages);
+  const int64_t r0 = batch * rank / nranks, r1 = batch * (rank + 1) / nranks;
+  p.row_begin = static_cast<int32_t>(r0);
+  p.block_table = block_table;
+  p.wait_ns = wait_ns > 0 ? static_cast<uint64_t>(wait_ns) : ptx::kWaitTimeoutNs;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int launches = 0;
+  if (phases & 1) {
+    peer_signal_kernel<<<1, 64, 0, st>>>(p, 0);
+    ++launches;
+  }
+  if ((phases & 2) && r1 > r0) {
+    peer_merge_kernel<<<static_cast<unsigned>(r1 - r0), kMergeThreads, kMergeSmem, st>>>(p);
+    ++launches;
+  }
+  if (phases & 4) {
+    peer_signal_kernel<<<1, 64, 0, st>>>(p, 1);
+    ++launches;
+  }
+  if (phases & 8) {
+    peer_wait_kernel<<<1, 64, 0, st>>>(p, 1);
+    ++launches;
+  }
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  t_last_launches = launches;
   return DSA_OK;
 }
 
