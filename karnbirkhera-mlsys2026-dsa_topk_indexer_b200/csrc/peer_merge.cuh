@@ -100,8 +100,37 @@ __global__ void peer_wait_kernel(const PeerParams p, int which) {
   peer_wait_flags(reinterpret_cast<const uint32_t*>(base + p.lay.flags(which)), p.nranks, p.epoch, p.wait_ns);
 }
 
+// One list's eight entries of this thread ([8t, 8t+8) of the row), fetched
+// with four 16-byte loads that are all in flight at once: a list in a peer's
+// memory costs one NVLink round trip, not eight.
+struct PeerListRegs {
+  float4 s0, s1;
+  int4 p0, p1;
+};
+
+__device__ __forceinline__ PeerListRegs peer_fetch(const PeerParams& p, int r, int64_t row) {
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(p.bases[r]);
+  const float4* s = reinterpret_cast<const float4*>(base + p.lay.scores()) + (row + threadIdx.x * 8) / 4;
+  const int4* q = reinterpret_cast<const int4*>(base + p.lay.pos()) + (row + threadIdx.x * 8) / 4;
+  return PeerListRegs{s[0], s[1], q[0], q[1]};
+}
+
+// The keys of load_list (same packing, same treatment of out-of-range
+// positions) from fetched registers.
+__device__ __forceinline__ void peer_store_keys(const PeerListRegs& v, uint64_t* dst, int64_t key_cap) {
+  const float sc[8] = {v.s0.x, v.s0.y, v.s0.z, v.s0.w, v.s1.x, v.s1.y, v.s1.z, v.s1.w};
+  const int32_t ps[8] = {v.p0.x, v.p0.y, v.p0.z, v.p0.w, v.p1.x, v.p1.y, v.p1.z, v.p1.w};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool ok = ps[k] >= 0 && static_cast<int64_t>(ps[k]) < key_cap;
+    if (ps[k] >= 0 && !ok) atomicOr(&g_dsa_status, DSA_STATUS_BAD_PAGE);
+    dst[threadIdx.x * 8 + k] = ok ? pack_key(sc[k], static_cast<uint32_t>(ps[k])) : 0ull;
+  }
+}
+
 // One CTA (kMergeThreads) per merged row: row p.row_begin + blockIdx.x.
 __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(const PeerParams p) {
+  static_assert(kMergeThreads * 8 == kTopK, "eight entries of a list per thread");
   extern __shared__ __align__(16) uint8_t msmem[];
   uint64_t* cur = reinterpret_cast<uint64_t*>(msmem);
   uint64_t* nxt = cur + kTopK;
@@ -112,15 +141,16 @@ __global__ void __launch_bounds__(kMergeThreads) peer_merge_kernel(const PeerPar
   const int b = p.row_begin + static_cast<int>(blockIdx.x);
   const int64_t row = static_cast<int64_t>(b) * kTopK;
   const int64_t key_cap = static_cast<int64_t>(p.max_pages) * kPage;
-  auto list = [&](int r, uint64_t* dst) {
-    const uint8_t* base = reinterpret_cast<const uint8_t*>(p.bases[r]);
-    load_list(reinterpret_cast<const float*>(base + p.lay.scores()) + row,
-              reinterpret_cast<const int32_t*>(base + p.lay.pos()) + row, dst, key_cap);
-  };
-  list(0, cur);
+  // Lists 0 and 1 are fetched together; list j + 1 is in flight while list
+  // j is merged.
+  const PeerListRegs first = peer_fetch(p, 0, row);
+  PeerListRegs next = first;
+  if (p.nranks > 1) next = peer_fetch(p, 1, row);
+  peer_store_keys(first, cur, key_cap);
 #pragma unroll 1
   for (int j = 1; j < p.nranks; ++j) {
-    list(j, nxt);
+    peer_store_keys(next, nxt, key_cap);
+    if (j + 1 < p.nranks) next = peer_fetch(p, j + 1, row);
     __syncthreads();
     merge_top(cur, nxt, res);
     __syncthreads();
