@@ -101,3 +101,20 @@ def test_queue_apply_argument_errors(lib):
     assert lib.dsa_decode_queue_apply(ok, 4, ok, ok, 4, 8, ok, ok, 4, None) == 1   # record below the header
     assert lib.dsa_decode_queue_apply(ok, 64, ok, ok, 0, 8, ok, ok, 4, None) == 1  # no slots
     assert lib.dsa_decode_queue_apply(ok, 64, ok, ok, 4, 8, ok, ok, 0, None) == 1  # no batch rows
+
+
+def test_peer_merge_argument_errors(lib):
+    """The peer-exchange entry points reject bad arguments before any CUDA
+    call (no GPU needed)."""
+    P = ctypes.c_void_p
+    ok = P(16)
+    n = ctypes.c_int64(0)
+    assert lib.dsa_peer_region_bytes(0, ctypes.byref(n)) == 1
+    assert lib.dsa_peer_region_bytes(4, ctypes.byref(n)) == 0 and n.value == 3 * 4 * 2048 * 4 + 512
+    assert lib.dsa_peer_merge(None, 2, 0, 1, 4, ok, 8, 15, 0, None) == 1   # no bases
+    assert lib.dsa_peer_merge(ok, 0, 0, 1, 4, ok, 8, 15, 0, None) == 1     # no ranks
+    assert lib.dsa_peer_merge(ok, 2, 2, 1, 4, ok, 8, 15, 0, None) == 1     # rank >= nranks
+    assert lib.dsa_peer_merge(ok, 65, 0, 1, 4, ok, 8, 15, 0, None) == 1    # more than 64 ranks
+    assert lib.dsa_peer_merge(ok, 2, 0, 1, 4, ok, 8, 16, 0, None) == 1     # unknown phase bit
+    assert lib.dsa_peer_alloc(0, ctypes.byref(P()), ctypes.create_string_buffer(64)) == 1
+    assert lib.dsa_peer_open(None, ctypes.byref(P())) == 1

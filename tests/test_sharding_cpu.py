@@ -117,3 +117,19 @@ def test_key_ranges_cover_and_align(pkg, L, world):
         assert b == c and a <= b
     for a, _ in rs:
         assert a % 128 == 0
+
+
+def test_peer_exchange_needs_its_region():
+    """exchange="peer" without a PeerExchange is an error, not a silent
+    fallback to another exchange."""
+    import importlib
+    sh = importlib.import_module(package().__name__ + ".sharding")
+    with socket.socket() as so:
+        so.bind(("127.0.0.1", 0))
+        port = so.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError, match="PeerExchange"):
+            sh.key_sharded_topk(None, None, None, None, torch.zeros((1, 4), dtype=torch.int32), exchange="peer")
+    finally:
+        dist.destroy_process_group()
