@@ -11,7 +11,9 @@ host->device, top-K device->host inside the timed region; the paged K cache
 is the serving system's resident device state). Under torchrun the one
 global batch is split: decode configs by request (balanced by total length,
 no collective), the long-context config 4 along the key axis (partial top-K,
-NCCL exchange, merge); both are strong scaling (the global batch is fixed).
+then the candidate lists exchanged and merged over NVLink peer memory by the
+library's own kernels, or through NCCL with --exchange alltoall|allgather);
+both are strong scaling (the global batch is fixed).
 """
 import argparse
 import importlib
@@ -194,8 +196,9 @@ def main():
                          "queue and through the per-step graph runner")
     ap.add_argument("--attn-tokens", type=int, default=128, help="sparse_attention: query tokens per step")
     ap.add_argument("--tokens", type=int, default=1 << 20, help="cache_write: tokens per step")
-    ap.add_argument("--exchange", choices=["alltoall", "allgather", "peer"], default="alltoall",
-                    help="key-sharded configs at N>1: how the per-rank candidate lists meet")
+    ap.add_argument("--exchange", choices=["peer", "alltoall", "allgather"], default="peer",
+                    help="key-sharded configs at N>1: how the per-rank candidate lists meet (peer: NVLink "
+                         "peer memory, the library's own kernels; alltoall / allgather: NCCL)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
