@@ -2,9 +2,12 @@
 
 Decode batches split by request with no collective (`request_shards`).
 Long sequences split along the key axis: every rank scores its key range and
-keeps a best-2048 candidate list, the lists are all-gathered (NCCL over
-NVLink on GPUs) and merged (`key_sharded_topk`). The reference has no
-multi-GPU path; this is the partitioning its north star asks for.
+keeps a best-2048 candidate list, and the lists meet and are merged
+(`key_sharded_topk`): over NVLink peer memory by this library's own kernels
+(`PeerExchange`: each rank merges its share of the rows straight from every
+rank's lists and stores them into every rank's output), or through NCCL
+(all-to-all by row or all-gather, then the merge kernel). The reference has
+no multi-GPU path; this is the partitioning its north star asks for.
 """
 import torch
 
