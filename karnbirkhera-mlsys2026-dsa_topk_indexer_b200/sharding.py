@@ -117,6 +117,9 @@ class PeerExchange:
         """One step of the protocol (all phases by default) on the current
         stream; returns `out`."""
         import ctypes
+        if (block_table.dim() != 2 or block_table.shape[0] != self.batch or block_table.dtype != torch.int32
+                or block_table.device != self.device):
+            raise RuntimeError(f"block_table must be int32 [{self.batch}, max_pages] on {self.device}")
         if phases & 1:
             self.epoch += 1
         bt = block_table.contiguous()
