@@ -80,6 +80,8 @@ class PeerExchange:
         self.pkg = importlib.import_module(__package__)
         self.lib = self.pkg._lib.load()
         self.group, self.device, self.batch, self.wait_ns = group, torch.device(device), int(batch), int(wait_ns)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         self.pkg._select(self.lib, self.device)
         nbytes = ctypes.c_int64(0)
